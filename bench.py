@@ -1,0 +1,442 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 sparse top-K decode attention (one JSON line on rank 0).
+
+Workload (the metric's configuration): one decode layer-step with
+B=4, N=32768, 32 query / 8 KV heads, head_dim 64, fp16 KV cache and Q, c=0.15 ->
+k_eff = adaptive_k_window(64, 32768, 0.15) = 4916 (the reference's rounding
+writes 4915). Each step uses a fresh Q and one of 4 distinct layer caches in rotation
+(4 x 268 MB, so consecutive steps never find their cache in the 126 MB L2). Synthetic,
+seeded inputs with the reference's sink / outlier-channel distribution.
+
+Metric: microseconds per layer-step (lower is better). ``value`` is device time of the
+timed K steps (max over ranks) divided by the steps of all ranks. With N GPUs every rank
+runs its own shard of (b, h_kv) units of the same size (weak scaling, no collective on the
+data path). Also reported: per-kernel times from CUDA events inside a second, instrumented
+timed loop; the roofline of the dominant kernel against the measured HBM bandwidth; the
+end-to-end time through the public API with host buffers; the CPU baseline (the C oracle,
+a restatement of the reference's algorithm, on the host cores).
+
+``--impl reference`` times the reference algorithm on the host CPU instead (the C oracle
+with all host threads; the reference itself is Python and does not travel to the box).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "dcr-attention_v3_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+CFG = dict(B=4, H=32, H_kv=8, N=32768, D=64, coverage=0.15, dtype="f16")
+METRIC = "sparse decode-attn us/layer (N=32K,B=4,c=.15)"
+UNIT = "us/layer"
+LAYERS = 4  # distinct layer caches rotated through
+
+
+def _k_eff(N, c):
+    from dcr_b200.models.llama.adaptive import adaptive_k_window
+    return adaptive_k_window(64, N, c)
+
+
+def _env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------------
+# CPU baseline: the C oracle (restatement of the reference's algorithm), all host threads
+# ---------------------------------------------------------------------------------------
+def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s, max_groups=None):
+    """Seconds per full layer-step of the C oracle, timed on a bounded sample of the
+    layer's batch rows and scaled by rows (the work is linear in B)."""
+    import numpy as np
+    import torch
+    from dcr_b200.synthetic import make_decode_inputs
+    from oracle import oracle
+
+    oracle.build()
+    torch_dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype_name]
+    b_sample = 1  # one batch row (8 KV heads, 32 query heads) per sample
+    Q, K, V = make_decode_inputs(b_sample, H, H_kv, N, dtype=torch_dt, seed=seed)
+
+    def bits(t):
+        t = t.contiguous()
+        return t.numpy() if t.dtype == torch.float32 else t.view(torch.int16).numpy().view(np.uint16)
+
+    q, kk, vv = bits(Q), bits(K), bits(V)
+    oracle.decode(q, kk, vv, dtype_name, k)  # warm-up
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 2:
+        t0 = time.perf_counter()
+        oracle.decode(q, kk, vv, dtype_name, k)
+        times.append(time.perf_counter() - t0)
+    per_layer = statistics.median(times) * (B / b_sample)
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    return per_layer, threads, len(times), b_sample
+
+
+def run_reference_arm(args):
+    rank, world, _ = _env()
+    if rank != 0:
+        return 0
+    B, H, H_kv, N = CFG["B"], CFG["H"], CFG["H_kv"], CFG["N"]
+    k = _k_eff(N, CFG["coverage"])
+    # each step = one sample (batch row 0) of the layer; value scaled to the full layer
+    import torch
+    from dcr_b200.synthetic import make_decode_inputs
+    from oracle import oracle
+    oracle.build()
+    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+    Q, K, V = make_decode_inputs(1, H, H_kv, N, dtype=torch.float16, seed=0)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view("uint16")  # noqa: E731
+    q, kk, vv = bits(Q), bits(K), bits(V)
+    for _ in range(args.warmup):
+        oracle.decode(q, kk, vv, "f16", k)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.decode(q, kk, vv, "f16", k)
+    dt = (time.perf_counter() - t0) / args.steps * B  # scale one batch row to B rows
+    value = dt * 1e6
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(value / 1e3, 4), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "config1 hero single-layer decode", "B": B, "N": N, "H": H,
+                   "H_kv": H_kv, "D": 64, "k_eff": k, "coverage": CFG["coverage"],
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads,
+                         "kind": "port",
+                         "sample": "C oracle (oracle/dcr_oracle.c, OpenMP) restating "
+                                   "topk_qaxis_attention_reference; each step = batch row 0 "
+                                   "(32 q-heads, N=32768) scaled x4 to the B=4 layer"},
+        "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------------------
+def _read_profile_traffic(kernel: str):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/), if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_hero.md")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        p = json.load(open(path))
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run_gpu_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200 import _lib
+    from dcr_b200.kernel.cuda import topk_qaxis_attention
+    from dcr_b200.kernel.cuda._common import workspace_bytes
+    from dcr_b200.synthetic import fresh_queries, make_decode_inputs
+
+    rank, world, local = _env()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    dev = torch.device("cuda", local if world > 1 else 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+
+    B, H, H_kv, N, D = CFG["B"], CFG["H"], CFG["H_kv"], CFG["N"], CFG["D"]
+    k = _k_eff(N, CFG["coverage"])
+    dt = torch.float16
+    dcode = _lib.DTYPE_CODES[dt]
+    eb = 2
+    steps, warm = args.steps, args.warmup
+
+    # layer caches (distinct per rank: seed = rank * 100 + layer)
+    caches = []
+    for L in range(LAYERS):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + L)
+        _, K, V = make_decode_inputs(B, H, H_kv, N, dtype=dt, device=dev, generator=g)
+        caches.append((K, V))
+    Qs = fresh_queries(max(steps, warm) + 1, B, H, dtype=dt, seed=7 + rank, device=dev)
+    ws_n = workspace_bytes(B, H, H_kv, N, k)
+    ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+    O = torch.empty(B, H, D, dtype=dt, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    ksb, ksh = H_kv * N * D, N * D
+
+    def step(i):
+        K, V = caches[i % LAYERS]
+        st = lib.dcr_decode(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), V.data_ptr(), dcode,
+                            ksb, ksh, ksb, ksh, B, H, H_kv, N, D, k, 1e-12, O.data_ptr(),
+                            ws.data_ptr(), ws_n, sp)
+        if st:
+            raise _lib.DCRError(st, "dcr_decode")
+
+    # separate buffers for the instrumented per-pass loop
+    rows = B * H
+    n_pad = (N + 7) // 8 * 8
+    scores = torch.empty(rows, n_pad, dtype=torch.bfloat16, device=dev)
+    idx = torch.empty(rows, k, dtype=torch.int32, device=dev)
+
+    def step_instrumented(i, ev):
+        K, V = caches[i % LAYERS]
+        q = Qs[i % Qs.shape[0]]
+        ev[0].record(stream)
+        st = lib.dcr_score(K.data_ptr(), dcode, ksb, ksh, None, q.data_ptr(), 1e-12, B, H, H_kv,
+                           N, D, scores.data_ptr(), n_pad, sp)
+        ev[1].record(stream)
+        st |= lib.dcr_select(scores.data_ptr(), n_pad, rows, N, k, idx.data_ptr(), sp)
+        ev[2].record(stream)
+        st |= lib.dcr_attend(q.data_ptr(), K.data_ptr(), V.data_ptr(), dcode, ksb, ksh, ksb, ksh,
+                             idx.data_ptr(), B, H, H_kv, N, D, k, O.data_ptr(), ws.data_ptr(),
+                             ws_n, sp)
+        ev[3].record(stream)
+        if st:
+            raise _lib.DCRError(st, "per-pass step")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # warm-up
+    for i in range(warm):
+        step(i)
+    barrier()
+    if _lib.read_device_status(clear=True):
+        raise RuntimeError("device status raised during warm-up")
+
+    gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(dev.index)).split(",")[dev.index]) \
+        if os.environ.get("CUDA_VISIBLE_DEVICES") else dev.index
+    with ClockSampler(gpu_index) as clk:
+        # soak so the clock sampler sees the GPU under this load (not timed)
+        t_soak = time.perf_counter() + args.soak
+        i = 0
+        while time.perf_counter() < t_soak:
+            step(i)
+            i += 1
+            if i % 64 == 0:
+                torch.cuda.synchronize(dev)
+        barrier()
+        # ---- timed region: exactly `steps` decode steps --------------------------------
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for i in range(steps):
+            step(i)
+        e1.record(stream)
+        barrier()
+        ms = e0.elapsed_time(e1)
+    clocks = clk.summary()
+
+    # ---- instrumented loop: per-kernel CUDA events (same stream) -----------------------
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    barrier()
+    for i in range(steps):
+        step_instrumented(i, evs[i])
+    barrier()
+    p1 = statistics.mean(e[0].elapsed_time(e[1]) for e in evs) * 1e3
+    p2 = statistics.mean(e[1].elapsed_time(e[2]) for e in evs) * 1e3
+    p3 = statistics.mean(e[2].elapsed_time(e[3]) for e in evs) * 1e3
+    status = _lib.read_device_status(clear=True)
+
+    # union of the selected rows per (b, h_kv): Pass 3's algorithmic K/V bytes
+    G = H // H_kv
+    union_rows = 0
+    for i in range(min(steps, 8)):
+        K, V = caches[i % LAYERS]
+        q = Qs[i % Qs.shape[0]]
+        lib.dcr_select_indices(q.data_ptr(), K.data_ptr(), dcode, ksb, ksh, B, H, H_kv, N, D, k,
+                               1e-12, idx.data_ptr(), ws.data_ptr(), ws_n, sp)
+        m = torch.zeros(B * H_kv, N, dtype=torch.bool, device=dev)
+        m.view(B, H_kv, N).scatter_(2, idx.view(B, H_kv, G * k).long(), True)
+        union_rows += int(m.sum())
+    union_rows /= min(steps, 8)
+
+    bytes_p1 = B * H_kv * N * D * eb + B * H * N * 2 + B * H * D * eb
+    bytes_p2 = B * H * N * 2 + B * H * k * 4
+    bytes_p3 = union_rows * 2 * D * eb + B * H * k * 4 + 2 * B * H * D * eb
+    peak, peak_kind = _peaks()
+    kern = {
+        "pass1_score": {"us": round(p1, 2), "bytes": bytes_p1, "gbs": round(bytes_p1 / p1 / 1e3, 1)},
+        "pass2_select": {"us": round(p2, 2), "bytes": bytes_p2, "gbs": round(bytes_p2 / p2 / 1e3, 1)},
+        "pass3_attend": {"us": round(p3, 2), "bytes": int(bytes_p3),
+                         "gbs": round(bytes_p3 / p3 / 1e3, 1),
+                         "union_rows_per_step": int(union_rows),
+                         "per_head_rows_per_step": B * H * k},
+    }
+    for v in kern.values():
+        v["frac_of_hbm"] = round(v["gbs"] / peak, 3)
+    dom_name = max(kern, key=lambda n: kern[n]["us"])
+    dom = kern[dom_name]
+    traffic = _read_profile_traffic(dom_name)
+
+    # ---- end to end through the public API with host buffers ---------------------------
+    Qh = Qs[:steps].cpu().pin_memory()
+    Oh = torch.empty(steps, B, H, D, dtype=dt).pin_memory()
+    Qd = torch.empty(B, H, D, dtype=dt, device=dev)
+    for i in range(3):
+        Qd.copy_(Qh[i], non_blocking=True)
+        topk_qaxis_attention(Qd, *caches[i % LAYERS], k, out=O, workspace_buf=ws)
+        Oh[i].copy_(O, non_blocking=True)
+        stream.synchronize()
+    barrier()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(steps):
+        Qd.copy_(Qh[i], non_blocking=True)                       # H2D of this step's query
+        topk_qaxis_attention(Qd, *caches[i % LAYERS], k, out=O, workspace_buf=ws)
+        Oh[i].copy_(O, non_blocking=True)                         # D2H of this step's output
+        stream.synchronize()                                      # the host reads O
+    f1.record(stream)
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(t[0]), float(t[1])
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        per_layer, threads, n, bs = cpu_reference_time(B, H, H_kv, N, k, CFG["dtype"], 0,
+                                                       budget_s=args.cpu_budget)
+        cpu = {"value": round(per_layer * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"C oracle (oracle/dcr_oracle.c, OpenMP, restating the reference's "
+                         f"topk_qaxis_attention_reference) on batch row 0 of the layer "
+                         f"(32 q-heads, N={N}), median of {n} runs over ~{args.cpu_budget:.0f} s, "
+                         f"scaled x{B // bs} to the B={B} layer"}
+
+    value = ms * 1e3 / (steps * world)
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 5),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": "config1 hero single-layer decode (fresh Q per step)",
+                   "B_per_rank": B, "N": N, "H": H, "H_kv": H_kv, "D": D, "k_eff": k,
+                   "coverage": CFG["coverage"],
+                   "parallelism": f"{world} rank(s), each its own (b, h_kv) shard" if world > 1
+                   else "single GPU",
+                   "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
+                         f"{2 * B * H_kv * N * D * eb / 1e6:.0f} MB",
+                   "clock_soak_s": args.soak},
+        "roofline": {"kernel": dom_name, "bound": "hbm", "achieved": dom["gbs"], "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": round(dom["gbs"] / peak, 3),
+                     "traffic": traffic, "algorithmic_bytes": dom["bytes"]},
+        "kernels": kern,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_ms * 1e3 / (steps * world), 3), "unit": UNIT,
+                "h2d_bytes_per_step": B * H * D * eb, "d2h_bytes_per_step": B * H * D * eb,
+                "api": "dcr_b200.kernel.cuda.topk_qaxis_attention, pinned host Q in / O out, "
+                       "host sync per step"},
+        "gpu_launches": 3 * steps,
+        "device_status": status,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--soak", type=float, default=1.5, help="untimed seconds before timing")
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

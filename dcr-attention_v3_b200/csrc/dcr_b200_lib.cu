@@ -1,0 +1,7 @@
+// dcr_b200_lib.cu — the single translation unit of libdcr_b200.so.
+// The kernels share one device status word (g_device_status, dcr_common.cuh); building
+// them as one unit keeps that a plain __device__ variable without relocatable device code.
+#include "dcr_score.cu"
+#include "dcr_select.cu"
+#include "dcr_attend.cu"
+#include "dcr_capi.cu"

@@ -1,0 +1,284 @@
+// dcr_capi.cu — extern "C" entry points of libdcr_b200 (declared in include/dcr_b200.h).
+//
+// This layer validates arguments the way the reference's Python wrappers do
+// (dcr_attention/kernel/triton/topk_axis.py:37-44, topk_axis_pass1.py:114-130,
+// topk_axis_pass2.py:30-36, fused_attn.py:170-193), lays out the caller's workspace and
+// enqueues the kernels on the caller's stream. It allocates nothing and never
+// synchronises (except dcr_read_device_status, a diagnostic).
+#include <cuda_runtime.h>
+
+#include <math.h>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "dcr_b200.h"
+#include "dcr_common.cuh"
+#include "dcr_internal.h"
+
+namespace dcr {
+
+int device_sm_count() {
+  static int cache[128] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+cudaError_t ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({func, dev})) return cudaSuccess;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert({func, dev});
+  return e;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+WorkspaceLayout workspace_layout(int rows, int N, int k_eff) {
+  WorkspaceLayout w;
+  w.splits = attend_splits(rows, k_eff);
+  w.n_pad = (static_cast<int64_t>(N) + 7) / 8 * 8;
+  size_t off = 0;
+  w.counters = off;
+  off = align_up(off + sizeof(int) * static_cast<size_t>(rows), 256);
+  w.partials = off;
+  off = align_up(off + sizeof(float) * static_cast<size_t>(rows) * w.splits * (kD + 2), 256);
+  w.scores = off;
+  off = align_up(off + sizeof(uint16_t) * static_cast<size_t>(rows) * w.n_pad, 256);
+  w.idx = off;
+  off = align_up(off + sizeof(int32_t) * static_cast<size_t>(rows) * k_eff, 256);
+  w.total = off;
+  return w;
+}
+
+}  // namespace dcr
+
+using namespace dcr;
+
+namespace {
+
+size_t dtype_bytes(int dtype) {
+  switch (dtype) {
+    case DCR_DTYPE_BF16:
+    case DCR_DTYPE_F16: return 2;
+    case DCR_DTYPE_F32: return 4;
+    default: return 0;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_heads(int B, int H, int H_kv, int N, int D) {
+  if (B <= 0 || H <= 0 || H_kv <= 0 || N <= 0) return DCR_ERR_SHAPE;
+  if (D != kD) return DCR_ERR_SHAPE;
+  if (H % H_kv != 0) return DCR_ERR_SHAPE;
+  const int G = H / H_kv;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return DCR_ERR_SHAPE;
+  if (static_cast<int64_t>(B) * H * kD > 0x7fffffffLL) return DCR_ERR_SHAPE;
+  return DCR_OK;
+}
+
+// The stride of a size-1 dimension never enters an address; replace it by the natural one
+// so that tensor-map encoding (which checks every stride) accepts views with odd strides
+// there (torch gives size-1 dims arbitrary strides).
+void normalize_strides(int64_t& sb, int64_t& sh, int B, int H_kv, int N) {
+  if (H_kv == 1) sh = static_cast<int64_t>(N) * kD;
+  if (B == 1) sb = sh * H_kv;
+}
+
+int check_cache(const void* C, int dtype, int64_t& sb, int64_t& sh, int B, int H_kv, int N) {
+  if (C == nullptr) return DCR_ERR_NULL;
+  normalize_strides(sb, sh, B, H_kv, N);
+  const size_t eb = dtype_bytes(dtype);
+  if (eb == 0) return DCR_ERR_DTYPE;
+  if (!aligned16(C)) return DCR_ERR_ALIGN;
+  if (sb < 0 || sh < 0) return DCR_ERR_SHAPE;
+  if ((sb * static_cast<int64_t>(eb)) % 16 != 0 || (sh * static_cast<int64_t>(eb)) % 16 != 0)
+    return DCR_ERR_ALIGN;
+  // rows of one head must not overlap the next head / batch entry
+  if (H_kv > 1 && sh < static_cast<int64_t>(N) * kD) return DCR_ERR_SHAPE;
+  if (B > 1 && sb < static_cast<int64_t>(N) * kD) return DCR_ERR_SHAPE;
+  return DCR_OK;
+}
+
+int check_k(int k_eff, int N) { return (k_eff > 0 && k_eff < N) ? DCR_OK : DCR_ERR_K_RANGE; }
+
+}  // namespace
+
+extern "C" {
+
+int dcr_version(void) { return DCR_ABI_VERSION; }
+
+const char* dcr_status_string(int status) {
+  switch (status) {
+    case DCR_OK: return "ok";
+    case DCR_ERR_NULL: return "a required pointer is NULL";
+    case DCR_ERR_SHAPE: return "unsupported shape or stride (D must be 64, H/H_kv in {1,2,4,8})";
+    case DCR_ERR_K_RANGE: return "k_eff must be in (0, N); caller must dispatch to SDPA";
+    case DCR_ERR_DTYPE: return "unknown dtype code";
+    case DCR_ERR_ALIGN: return "pointer or stride is not 16-byte aligned";
+    case DCR_ERR_WORKSPACE: return "workspace is NULL or smaller than dcr_workspace_bytes()";
+    case DCR_ERR_CUDA: return "a CUDA runtime call failed";
+    case DCR_ERR_DEVICE_TIMEOUT: return "device: a bounded wait expired";
+    case DCR_ERR_DEVICE_INDEX: return "device: an index outside [0, N) was skipped";
+    default: return "unknown status";
+  }
+}
+
+int dcr_adaptive_k_window(int k_window_min, int n_kv, double coverage_floor) {
+  // adaptive_k_window, dcr_attention/models/llama/adaptive.py:85-105
+  if (n_kv <= 0) return -1;
+  if (!(coverage_floor >= 0.0 && coverage_floor <= 1.0)) return -1;
+  const long long floor_value = static_cast<long long>(static_cast<double>(n_kv) * coverage_floor);
+  long long k = floor_value > k_window_min ? floor_value : k_window_min;
+  if (k > n_kv) k = n_kv;
+  if (k % 2 == 1) k = (k + 1 < n_kv) ? k + 1 : n_kv;
+  return static_cast<int>(k);
+}
+
+size_t dcr_workspace_bytes(int B, int H, int H_kv, int N, int D, int k_eff) {
+  if (check_heads(B, H, H_kv, N, D) != DCR_OK || k_eff <= 0) return 0;
+  return workspace_layout(B * H, N, k_eff).total;
+}
+
+int dcr_unit_query(const void* Q, int dtype, int B, int H, int D, float eps, float* u_out,
+                   void* stream) {
+  if (Q == nullptr || u_out == nullptr) return DCR_ERR_NULL;
+  if (dtype_bytes(dtype) == 0) return DCR_ERR_DTYPE;
+  if (B <= 0 || H <= 0 || D != kD) return DCR_ERR_SHAPE;
+  if (!aligned16(Q) || !aligned16(u_out)) return DCR_ERR_ALIGN;
+  return launch_unit_query(Q, dtype, B * H, eps, u_out, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h, const float* u,
+              const void* Q, float eps, int B, int H, int H_kv, int N, int D, uint16_t* scores,
+              int64_t s_stride_row, void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N);
+  if (st) return st;
+  if (scores == nullptr) return DCR_ERR_NULL;
+  if (u == nullptr && Q == nullptr) return DCR_ERR_NULL;
+  if (u != nullptr && !aligned16(u)) return DCR_ERR_ALIGN;
+  if (u == nullptr && !aligned16(Q)) return DCR_ERR_ALIGN;
+  if (s_stride_row < N) return DCR_ERR_SHAPE;
+  return launch_score(K, dtype, k_stride_b, k_stride_h, u, Q, eps, B, H, H_kv, N, scores,
+                      s_stride_row, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+               int32_t* idx_out, void* stream) {
+  if (scores == nullptr || idx_out == nullptr) return DCR_ERR_NULL;
+  if (rows <= 0 || N <= 0 || s_stride_row < N) return DCR_ERR_SHAPE;
+  int st = check_k(k_eff, N);
+  if (st) return st;
+  return launch_select(scores, s_stride_row, rows, N, k_eff, idx_out, nullptr,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int dcr_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+               int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, const int32_t* idx,
+               int B, int H, int H_kv, int N, int D, int k_eff, void* O, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
+  if ((st = check_cache(V, dtype, v_stride_b, v_stride_h, B, H_kv, N))) return st;
+  if (Q == nullptr || O == nullptr || idx == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q) || !aligned16(O)) return DCR_ERR_ALIGN;
+  if ((st = check_k(k_eff, N))) return st;
+  const int rows = B * H;
+  const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* partials = nullptr;
+  int* counters = nullptr;
+  if (w.splits > 1) {
+    if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    partials = reinterpret_cast<float*>(ws + w.partials);
+    counters = reinterpret_cast<int*>(ws + w.counters);
+    if (cudaMemsetAsync(counters, 0, sizeof(int) * rows, s) != cudaSuccess) return DCR_ERR_CUDA;
+  }
+  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B,
+                       H, H_kv, N, k_eff, O, w.splits, partials, counters, s);
+}
+
+int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride_b,
+                       int64_t k_stride_h, int B, int H, int H_kv, int N, int D, int k_eff,
+                       float eps, int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
+  if (Q == nullptr || idx_out == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q)) return DCR_ERR_ALIGN;
+  if ((st = check_k(k_eff, N))) return st;
+  const int rows = B * H;
+  const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
+  if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
+                         w.n_pad, s)))
+    return st;
+  return launch_select(scores, w.n_pad, rows, N, k_eff, idx_out, nullptr, s);
+}
+
+int dcr_decode(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+               int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, int B, int H,
+               int H_kv, int N, int D, int k_eff, float eps, void* O, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
+  if ((st = check_cache(V, dtype, v_stride_b, v_stride_h, B, H_kv, N))) return st;
+  if (Q == nullptr || O == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q) || !aligned16(O)) return DCR_ERR_ALIGN;
+  if ((st = check_k(k_eff, N))) return st;
+  const int rows = B * H;
+  const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
+  if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
+  int32_t* idx = reinterpret_cast<int32_t*>(ws + w.idx);
+  int* counters = reinterpret_cast<int*>(ws + w.counters);
+  float* partials = reinterpret_cast<float*>(ws + w.partials);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
+                         w.n_pad, s)))
+    return st;
+  // Pass 2 also resets the Pass 3 split-K tickets of its row.
+  if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, idx, counters, s))) return st;
+  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B, H,
+                       H_kv, N, k_eff, O, w.splits, partials, counters, s);
+}
+
+int dcr_read_device_status(int* status_out, int clear) {
+  if (status_out == nullptr) return DCR_ERR_NULL;
+  if (cudaDeviceSynchronize() != cudaSuccess) return DCR_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, dcr::g_device_status, sizeof(int)) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  *status_out = v;
+  if (clear) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(dcr::g_device_status, &zero, sizeof(int)) != cudaSuccess)
+      return DCR_ERR_CUDA;
+  }
+  return DCR_OK;
+}
+
+}  // extern "C"

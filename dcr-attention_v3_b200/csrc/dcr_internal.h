@@ -1,0 +1,49 @@
+// dcr_internal.h — launch helpers shared by the translation units of libdcr_b200.
+// Every launcher validates nothing (the C-ABI layer in dcr_capi.cu does) and returns a
+// dcr_status code (DCR_ERR_CUDA when a launch fails).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "dcr_b200.h"
+
+namespace dcr {
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+// Sets the dynamic shared-memory limit of a kernel once per (kernel, device).
+cudaError_t ensure_smem_attr(const void* func, int bytes);
+
+// Split-K factor used by Pass 3 for this shape (1 = no split, no workspace partials).
+int attend_splits(int rows, int k_eff);
+
+// Workspace layout shared by dcr_decode / dcr_select_indices / dcr_attend.
+struct WorkspaceLayout {
+  size_t counters;  // int32 [rows]
+  size_t partials;  // fp32 [rows * splits * (D + 2)]
+  size_t scores;    // uint16 [rows * n_pad]
+  size_t idx;       // int32 [rows * k_eff]
+  size_t total;
+  int splits;
+  int64_t n_pad;
+};
+WorkspaceLayout workspace_layout(int rows, int N, int k_eff);
+
+int launch_unit_query(const void* Q, int dtype, int rows, float eps, float* u, cudaStream_t st);
+
+int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
+                 const float* u, const void* Q, float eps, int B, int H, int H_kv, int N,
+                 uint16_t* scores, int64_t s_stride_row, cudaStream_t st);
+
+int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+                  int32_t* idx, int* row_counters, cudaStream_t st);
+
+int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+                  int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,
+                  const int32_t* idx, int B, int H, int H_kv, int N, int k_eff, void* O,
+                  int splits, float* partials, int* counters, cudaStream_t st);
+
+}  // namespace dcr

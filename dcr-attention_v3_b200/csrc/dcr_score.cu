@@ -1,0 +1,356 @@
+// dcr_score.cu — unit query and Pass 1 (projection scores) for sm_100a.
+//
+// Pass 1 replaces the reference's _pass1_projection_kernel
+// (dcr_attention/kernel/triton/topk_axis_pass1.py:29) and its oracle
+// _compute_projection_scores (dcr_attention/kernel/qaxis_topk_reference.py:58):
+//     score[b, h, n] = bf16_rne( sum_d f32(K[b, h / G, n, d]) * u[b, h, d] ).
+// The unit query replaces _compute_u_Q (qaxis_topk_reference.py:42):
+//     u = f32(q) / max(||f32(q)||_2, eps).
+//
+// Design (B200): the pass is a pure HBM stream of the K cache (128 B per row for 16-bit
+// caches) with G = H / H_kv query heads scored per row. A persistent grid of
+// 2 CTAs per SM walks contiguous ranges of row tiles; one thread per CTA issues 4-D TMA
+// tile loads (128-byte swizzle) into a 3-stage shared-memory ring completed by
+// mbarriers, and every thread scores RPT rows of each tile against the G unit queries of
+// the tile's (b, h_kv) group. The fp32 dot product of every (row, head) runs
+// d = 0..63 as one chain of fused multiply-adds from 0, so a CPU restatement with
+// fmaf in the same order reproduces every score bit for bit.
+//
+// The unit query is computed by one warp per query row: lane l squares elements 2l and
+// 2l+1 (x0*x0 rounded, then fmaf(x1, x1, .)), the 32 partial sums are combined by an
+// xor butterfly (offsets 16, 8, 4, 2, 1), then u = x / max(sqrtf(sum), eps) with IEEE
+// sqrt and division.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "dcr_common.cuh"
+#include "dcr_internal.h"
+
+namespace dcr {
+
+// ---------------------------------------------------------------------------------------
+// Unit query
+// ---------------------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load_pair(const void* row, int lane, float& x0, float& x1) {
+  if constexpr (sizeof(T) == 4) {
+    const float2 v = reinterpret_cast<const float2*>(row)[lane];
+    x0 = v.x;
+    x1 = v.y;
+  } else {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(row)[lane];
+    const float2 v = ElemTraits<T>::widen2(w);
+    x0 = v.x;
+    x1 = v.y;
+  }
+}
+
+// One warp: u_row[0..63] = q_row / max(||q_row||, eps). All lanes of the warp must call.
+template <typename T>
+__device__ __forceinline__ void unit_query_warp(const void* q_row, float eps, float* u_row) {
+  const int lane = threadIdx.x & 31;
+  float x0, x1;
+  load_pair<T>(q_row, lane, x0, x1);
+  const float sq0 = x0 * x0;
+  float part = fmaf(x1, x1, sq0);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, off);
+  const float norm = fmaxf(sqrtf(part), eps);
+  u_row[2 * lane] = x0 / norm;
+  u_row[2 * lane + 1] = x1 / norm;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) unit_query_kernel(const void* __restrict__ q, int rows,
+                                                         float eps, float* __restrict__ u) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (warp >= rows) return;
+  const char* q_row = static_cast<const char*>(q) + static_cast<size_t>(warp) * kD * sizeof(T);
+  unit_query_warp<T>(q_row, eps, u + static_cast<size_t>(warp) * kD);
+}
+
+int launch_unit_query(const void* Q, int dtype, int rows, float eps, float* u, cudaStream_t st) {
+  const int threads = 128;
+  const int blocks = (rows * 32 + threads - 1) / threads;
+  switch (dtype) {
+    case DCR_DTYPE_BF16:
+      unit_query_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(Q, rows, eps, u);
+      break;
+    case DCR_DTYPE_F16:
+      unit_query_kernel<__half><<<blocks, threads, 0, st>>>(Q, rows, eps, u);
+      break;
+    default:
+      unit_query_kernel<float><<<blocks, threads, 0, st>>>(Q, rows, eps, u);
+      break;
+  }
+  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------------------
+// Pass 1
+// ---------------------------------------------------------------------------------------
+constexpr int kP1Threads = 128;
+constexpr int kP1Stages = 3;
+
+template <typename T>
+struct P1Cfg {
+  static constexpr int kRPT = (sizeof(T) == 4) ? 1 : 2;  // rows per thread per tile
+  static constexpr int kTileRows = kP1Threads * kRPT;   // 256 (16-bit) or 128 (fp32)
+  static constexpr int kStageBytes = kTileRows * RowTraits<T>::kRowBytes;  // 32 KiB
+  static constexpr int kBoxCols = 128 / ElemTraits<T>::kBytes;            // 64 or 32
+};
+
+template <typename T, int G>
+constexpr int p1_smem_bytes() {
+  return 1024 + kP1Stages * P1Cfg<T>::kStageBytes + G * kD * 4 + kP1Stages * 8;
+}
+
+struct P1Params {
+  const float* u;  // [rows_q, 64] fp32 or nullptr (then computed from q)
+  const void* q;   // [rows_q, 64] in the cache dtype
+  float eps;
+  uint16_t* scores;
+  int64_t s_stride;
+  int N;
+  int H_kv;
+  int tiles_per_group;
+  int total_tiles;
+};
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar,
+                                            int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+      : "memory");
+}
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kP1Threads, 2)
+    score_kernel(const __grid_constant__ CUtensorMap kmap, const P1Params p) {
+  using Cfg = P1Cfg<T>;
+  constexpr int kChunks = RowTraits<T>::kChunks;
+  constexpr int kPer = ElemTraits<T>::kPerChunk;
+  constexpr int kRPT = Cfg::kRPT;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* tiles = smem;
+  float* u_s = reinterpret_cast<float*>(smem + kP1Stages * Cfg::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(u_s + G * kD);
+
+  const int tid = threadIdx.x;
+  const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_tiles / gridDim.x);
+  const int t_end =
+      static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_tiles / gridDim.x);
+  const int my_tiles = t_end - t_begin;
+  if (my_tiles <= 0) return;
+
+  if (tid == 0) {
+    tma_prefetch_desc(&kmap);
+#pragma unroll
+    for (int s = 0; s < kP1Stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int it) {
+    const int t = t_begin + it;
+    const int s = it % kP1Stages;
+    const int g = t / p.tiles_per_group;
+    const int n0 = (t - g * p.tiles_per_group) * Cfg::kTileRows;
+    const int b = g / p.H_kv;
+    const int hk = g - b * p.H_kv;
+    uint8_t* dst = tiles + s * Cfg::kStageBytes;
+    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+#pragma unroll
+    for (int sub = 0; sub < RowTraits<T>::kSubTiles; ++sub)
+      tma_load_4d(dst + sub * Cfg::kTileRows * 128, &kmap, &full[s], sub * Cfg::kBoxCols, n0, hk,
+                  b);
+  };
+
+  if (tid == 0) {
+    const int pre = my_tiles < kP1Stages ? my_tiles : kP1Stages;
+    for (int it = 0; it < pre; ++it) issue(it);
+  }
+
+  int cur_group = -1;
+  for (int it = 0; it < my_tiles; ++it) {
+    const int t = t_begin + it;
+    const int s = it % kP1Stages;
+    const int g = t / p.tiles_per_group;
+    const int n0 = (t - g * p.tiles_per_group) * Cfg::kTileRows;
+
+    if (g != cur_group) {  // uniform across the CTA
+      __syncthreads();     // earlier readers of u_s are done
+      if (p.u != nullptr) {
+        for (int i = tid; i < G * kD; i += kP1Threads) u_s[i] = p.u[static_cast<size_t>(g) * G * kD + i];
+      } else {
+        const int warp = tid >> 5;
+        for (int j = warp; j < G; j += kP1Threads / 32) {
+          const char* q_row = static_cast<const char*>(p.q) +
+                              (static_cast<size_t>(g) * G + j) * kD * sizeof(T);
+          unit_query_warp<T>(q_row, p.eps, u_s + j * kD);
+        }
+      }
+      __syncthreads();
+      cur_group = g;
+    }
+
+    const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / kP1Stages) & 1));
+
+    const uint32_t tile_addr = smem_u32(tiles + s * Cfg::kStageBytes);
+    float acc[kRPT][G];
+#pragma unroll
+    for (int rr = 0; rr < kRPT; ++rr)
+#pragma unroll
+      for (int j = 0; j < G; ++j) acc[rr][j] = 0.0f;
+
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      float kf[kRPT][kPer];
+#pragma unroll
+      for (int rr = 0; rr < kRPT; ++rr) {
+        const int r = tid + rr * kP1Threads;
+        const uint4 v = lds128(tile_addr + swz_offset(r, c, Cfg::kTileRows));
+        ElemTraits<T>::widen(v, kf[rr]);
+      }
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        float uv[kPer];
+        const float4* u4 = reinterpret_cast<const float4*>(u_s + j * kD + c * kPer);
+#pragma unroll
+        for (int q4 = 0; q4 < kPer / 4; ++q4) {
+          const float4 t4 = u4[q4];
+          uv[4 * q4 + 0] = t4.x;
+          uv[4 * q4 + 1] = t4.y;
+          uv[4 * q4 + 2] = t4.z;
+          uv[4 * q4 + 3] = t4.w;
+        }
+#pragma unroll
+        for (int e = 0; e < kPer; ++e)
+#pragma unroll
+          for (int rr = 0; rr < kRPT; ++rr) acc[rr][j] = fmaf(kf[rr][e], uv[e], acc[rr][j]);
+      }
+    }
+
+#pragma unroll
+    for (int rr = 0; rr < kRPT; ++rr) {
+      const int n = n0 + tid + rr * kP1Threads;
+      if (n < p.N) {
+#pragma unroll
+        for (int j = 0; j < G; ++j)
+          p.scores[(static_cast<int64_t>(g) * G + j) * p.s_stride + n] = f32_to_bf16_bits(acc[rr][j]);
+      }
+    }
+
+    if (__syncthreads_or(!ok)) break;  // every thread is done reading stage s
+    if (tid == 0 && it + kP1Stages < my_tiles) {
+      fence_proxy_async_smem();
+      issue(it + kP1Stages);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Host side: tensor map + launch
+// ---------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+template <typename T, int G>
+static int launch_score_t(const void* K, int64_t ksb, int64_t ksh, const P1Params& p, int B,
+                          int H_kv, cudaStream_t st) {
+  using Cfg = P1Cfg<T>;
+  EncodeTiledFn encode = get_encode_fn();
+  if (!encode) return DCR_ERR_CUDA;
+  CUtensorMapDataType dt = sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                          : (std::is_same<T, __half>::value
+                                                 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(p.N),
+                              static_cast<cuuint64_t>(H_kv), static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD * sizeof(T)),
+                                 static_cast<cuuint64_t>(ksh * sizeof(T)),
+                                 static_cast<cuuint64_t>(ksb * sizeof(T))};
+  const cuuint32_t box[4] = {static_cast<cuuint32_t>(Cfg::kBoxCols),
+                             static_cast<cuuint32_t>(Cfg::kTileRows), 1u, 1u};
+  const cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUtensorMap map;
+  CUresult r = encode(&map, dt, 4, const_cast<void*>(K), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return DCR_ERR_CUDA;
+
+  constexpr int smem = p1_smem_bytes<T, G>();
+  if (ensure_smem_attr(reinterpret_cast<const void*>(&score_kernel<T, G>), smem) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  const int max_ctas = device_sm_count() * 2;
+  const int grid = p.total_tiles < max_ctas ? p.total_tiles : max_ctas;
+  score_kernel<T, G><<<grid, kP1Threads, smem, st>>>(map, p);
+  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+}
+
+template <typename T>
+static int launch_score_g(const void* K, int64_t ksb, int64_t ksh, const P1Params& p, int B,
+                          int H_kv, int G, cudaStream_t st) {
+  switch (G) {
+    case 1: return launch_score_t<T, 1>(K, ksb, ksh, p, B, H_kv, st);
+    case 2: return launch_score_t<T, 2>(K, ksb, ksh, p, B, H_kv, st);
+    case 4: return launch_score_t<T, 4>(K, ksb, ksh, p, B, H_kv, st);
+    case 8: return launch_score_t<T, 8>(K, ksb, ksh, p, B, H_kv, st);
+    default: return DCR_ERR_SHAPE;
+  }
+}
+
+int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
+                 const float* u, const void* Q, float eps, int B, int H, int H_kv, int N,
+                 uint16_t* scores, int64_t s_stride_row, cudaStream_t st) {
+  P1Params p;
+  p.u = u;
+  p.q = Q;
+  p.eps = eps;
+  p.scores = scores;
+  p.s_stride = s_stride_row;
+  p.N = N;
+  p.H_kv = H_kv;
+  const int G = H / H_kv;
+  const int tile_rows = dtype == DCR_DTYPE_F32 ? P1Cfg<float>::kTileRows
+                                               : P1Cfg<__nv_bfloat16>::kTileRows;
+  p.tiles_per_group = (N + tile_rows - 1) / tile_rows;
+  const int64_t total = static_cast<int64_t>(p.tiles_per_group) * B * H_kv;
+  if (total > 0x7fffffff) return DCR_ERR_SHAPE;
+  p.total_tiles = static_cast<int>(total);
+  switch (dtype) {
+    case DCR_DTYPE_BF16:
+      return launch_score_g<__nv_bfloat16>(K, k_stride_b, k_stride_h, p, B, H_kv, G, st);
+    case DCR_DTYPE_F16:
+      return launch_score_g<__half>(K, k_stride_b, k_stride_h, p, B, H_kv, G, st);
+    case DCR_DTYPE_F32:
+      return launch_score_g<float>(K, k_stride_b, k_stride_h, p, B, H_kv, G, st);
+    default:
+      return DCR_ERR_DTYPE;
+  }
+}
+
+}  // namespace dcr

@@ -1,0 +1,136 @@
+/*
+ * dcr_b200.h — C ABI of the B200 (sm_100a) sparse top-K decode-attention library
+ * (libdcr_b200.so).
+ *
+ * This is the drop-in boundary for DCR-Attention's per-step sparse decode attention.
+ * Each entry point replaces one function of the reference's Python kernel API; the
+ * comment above each declaration names the function it replaces (file:line within the
+ * Seqev/dcr-attention_v3 project).
+ *
+ * Conventions shared by every entry point
+ * ---------------------------------------
+ *  - All tensor arguments are DEVICE pointers owned by the caller. Inputs are only read.
+ *    Outputs are written in place; nothing is allocated by the library.
+ *  - Shapes follow the reference: Q and O are [B, H, D]; the KV caches are
+ *    [B, H_kv, N, D]; scores are [B*H, N]; indices are [B*H, k_eff] int32.
+ *    Query head h reads KV head h / (H / H_kv) (GQA).
+ *  - D must be 64 (DCR_HEAD_DIM) and H / H_kv must be 1, 2, 4 or 8.
+ *  - Cache rows must be contiguous (stride D along N, 1 along D). The batch and head
+ *    strides (in elements) are free, so a cache allocated for N_max >= N positions can
+ *    be passed directly. Every cache pointer and stride must be 16-byte aligned.
+ *  - dtype is one of dcr_dtype; Q, K and V share it. O is written in the same dtype.
+ *    Scores are always bfloat16 (raw bits, uint16), as in the reference.
+ *  - `stream` is a cudaStream_t cast to void* (NULL = legacy default stream). Calls are
+ *    asynchronous and stream ordered; nothing synchronises. Kernels never spin without a
+ *    bound; a wait that expires, or an index outside [0, N), sets a sticky device status
+ *    that dcr_read_device_status() returns.
+ *  - Return value: 0 (DCR_OK) or a dcr_status code. A non-zero code means nothing was
+ *    launched.
+ */
+#ifndef DCR_B200_H_
+#define DCR_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DCR_HEAD_DIM 64
+#define DCR_ABI_VERSION 1
+
+typedef enum dcr_dtype {
+  DCR_DTYPE_BF16 = 0,
+  DCR_DTYPE_F16 = 1,
+  DCR_DTYPE_F32 = 2
+} dcr_dtype;
+
+typedef enum dcr_status {
+  DCR_OK = 0,
+  DCR_ERR_NULL = 1,             /* a required pointer is NULL                         */
+  DCR_ERR_SHAPE = 2,            /* B, H, H_kv, N, D or a stride out of range          */
+  DCR_ERR_K_RANGE = 3,          /* k_eff not in (0, N): caller must dispatch to SDPA  */
+  DCR_ERR_DTYPE = 4,            /* unknown dtype code                                 */
+  DCR_ERR_ALIGN = 5,            /* pointer or stride not 16-byte aligned              */
+  DCR_ERR_WORKSPACE = 6,        /* workspace pointer NULL or smaller than required    */
+  DCR_ERR_CUDA = 7,             /* a CUDA runtime call failed                         */
+  DCR_ERR_DEVICE_TIMEOUT = 8,   /* device status: a bounded wait expired              */
+  DCR_ERR_DEVICE_INDEX = 16     /* device status: an index outside [0, N) was skipped */
+} dcr_status;
+
+/* Library ABI version (DCR_ABI_VERSION). */
+int dcr_version(void);
+
+/* Human-readable text for a dcr_status code (static storage). */
+const char* dcr_status_string(int status);
+
+/* k_eff = min(N, max(k_min, floor(N * c))), rounded up to even and capped at N.
+ * Replaces adaptive_k_window, dcr_attention/models/llama/adaptive.py:39.
+ * Returns -1 when n_kv <= 0 or c is outside [0, 1]. */
+int dcr_adaptive_k_window(int k_window_min, int n_kv, double coverage_floor);
+
+/* Bytes of workspace dcr_decode / dcr_select_indices / dcr_attend need for this shape
+ * (a superset for all three). Returns 0 for an invalid shape. */
+size_t dcr_workspace_bytes(int B, int H, int H_kv, int N, int D, int k_eff);
+
+/* u = f32(Q) / max(||f32(Q)||_2, eps), fp32 [B, H, D].
+ * Replaces _compute_u_Q, dcr_attention/kernel/qaxis_topk_reference.py:42
+ * (called by topk_qaxis_select, dcr_attention/kernel/triton/topk_axis.py:47). */
+int dcr_unit_query(const void* Q, int dtype, int B, int H, int D, float eps,
+                   float* u_out, void* stream);
+
+/* Pass 1: scores[b*H + h, n] = bf16_rne(sum_d f32(K[b, h/G, n, d]) * u[b, h, d]).
+ * The fp32 sum runs d = 0..63 as a chain of fused multiply-adds.
+ * If u is NULL the unit query is computed from Q (same dtype as K) with eps.
+ * Replaces topk_pass1_projection, dcr_attention/kernel/triton/topk_axis_pass1.py:104
+ * (kernel _pass1_projection_kernel, topk_axis_pass1.py:29). */
+int dcr_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
+              const float* u, const void* Q, float eps,
+              int B, int H, int H_kv, int N, int D,
+              uint16_t* scores, int64_t s_stride_row, void* stream);
+
+/* Pass 2: per row, the k_eff indices of the largest bf16 scores (ties: lower index
+ * first), written in ascending index order as int32. -0 equals +0; NaN ranks highest.
+ * Replaces topk_pass2_select, dcr_attention/kernel/triton/topk_axis_pass2.py:16. */
+int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+               int32_t* idx_out, void* stream);
+
+/* Pass 3: O[b, h] = softmax((K[b, h/G, idx] . f32(Q[b, h])) / sqrt(D)) @ V[b, h/G, idx],
+ * fp32 online softmax, one rounding to the output dtype. idx is [B*H, k_eff] int32.
+ * Replaces fused_topk_attention, dcr_attention/kernel/triton/fused_attn.py:158
+ * (kernel _pass3_fused_attn_kernel, fused_attn.py:40). */
+int dcr_attend(const void* Q, const void* K, const void* V, int dtype,
+               int64_t k_stride_b, int64_t k_stride_h,
+               int64_t v_stride_b, int64_t v_stride_h,
+               const int32_t* idx, int B, int H, int H_kv, int N, int D, int k_eff,
+               void* O, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Pass 1 + Pass 2: u_Q, scores and the top-K indices [B*H, k_eff] int32 ascending.
+ * Replaces topk_qaxis_select, dcr_attention/kernel/triton/topk_axis.py:20. */
+int dcr_select_indices(const void* Q, const void* K, int dtype,
+                       int64_t k_stride_b, int64_t k_stride_h,
+                       int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                       int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Full decode step (Pass 1 + 2 + 3): O [B, H, D] from Q, K, V and k_eff.
+ * Replaces topk_qaxis_attention, dcr_attention/kernel/triton/topk_axis.py:58
+ * (and its oracle topk_qaxis_attention_reference,
+ *  dcr_attention/kernel/qaxis_topk_reference.py:200). */
+int dcr_decode(const void* Q, const void* K, const void* V, int dtype,
+               int64_t k_stride_b, int64_t k_stride_h,
+               int64_t v_stride_b, int64_t v_stride_h,
+               int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+               void* O, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Synchronises the current device and returns (in *status_out) the OR of the device
+ * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.
+ * Diagnostic: the reference has no counterpart (its kernels have no device status). */
+int dcr_read_device_status(int* status_out, int clear);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* DCR_B200_H_ */

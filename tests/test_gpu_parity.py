@@ -1,0 +1,279 @@
+"""Parity of the CUDA path (through the C ABI) with the reference and the oracle (B200).
+
+Gates (north star + the reference's own kernel_spec.md section 5):
+* unit query, Pass 1 scores, Pass 2 / end-to-end indices: bit-exact against the oracle;
+  indices also bit-exact against the reference's golden vectors;
+* Pass 1 scores vs the reference's einsum: at most one bf16 ulp, RMSE^2 <= 1e-6;
+* attention outputs: max|d| <= 2e-3 beyond the output rounding, cosine >= 0.9999,
+  RMSE^2 <= 1e-6 against the reference's unrounded fp32 output (or the oracle's).
+At full size (3 and one GPU's shard of config 4) the oracle is run too,
+and the size-independent properties of an exact top-K are checked on the device.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import ALL_CASES, attention_close, bf16_bits_to_f32, dtype_name, load_case, to_np
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(cuda_lib):
+    from dcr_b200 import _lib
+    _lib.read_device_status(clear=True)
+    yield
+    assert _lib.read_device_status(clear=True) == 0, "a kernel raised a device status"
+
+
+def _api():
+    from dcr_b200.kernel import cuda as api
+    return api
+
+
+def _bf16_tensor(bits: np.ndarray, shape) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16).reshape(shape)
+
+
+# ---------------------------------------------------------------------------------------
+# Golden vectors (made by the reference itself)
+# ---------------------------------------------------------------------------------------
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_unit_query_bit_exact(oracle_mod, name):
+    meta, (Q, K, V), g = load_case(name)
+    u = _api().compute_u_Q(Q.to(DEV)).cpu().numpy()
+    assert np.array_equal(u.view(np.uint32), oracle_mod.unit_query(to_np(Q), dtype_name(Q)).view(np.uint32))
+    ulp = np.spacing(np.abs(g["u"]).astype(np.float32))
+    assert np.all(np.abs(u - g["u"]) <= 2 * ulp + 1e-30)
+
+
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_pass1_scores(oracle_mod, name):
+    meta, (Q, K, V), g = load_case(name)
+    B, H, N = meta["B"], meta["H"], meta["N"]
+    s = _api().topk_pass1_projection(K.to(DEV), torch.from_numpy(g["u"]).to(DEV))
+    assert s.shape == (B, H, N) and s.dtype == torch.bfloat16
+    bits = to_np(s).reshape(B * H, N)
+    want_oracle = oracle_mod.scores(to_np(K), dtype_name(K), g["u"])
+    assert np.array_equal(bits, want_oracle), "Pass 1 scores differ from the oracle's bits"
+    got, ref = bf16_bits_to_f32(bits), bf16_bits_to_f32(g["scores"])
+    d = np.abs(got - ref)
+    assert d.max() <= 1e-2 and (d ** 2).mean() <= 1e-6          # reference gate
+    assert np.all(d <= np.spacing(np.abs(ref)) * 2 ** 16 + 1e-30)  # <= one bf16 ulp
+
+
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_pass2_bit_exact_on_reference_scores(name):
+    meta, _, g = load_case(name)
+    B, H, N, k = meta["B"], meta["H"], meta["N"], meta["k"]
+    idx = _api().topk_pass2_select(_bf16_tensor(g["scores"], (B, H, N)).to(DEV), k)
+    assert idx.dtype == torch.int32 and idx.shape == (B, H, k)
+    assert np.array_equal(idx.cpu().numpy().reshape(B * H, k), g["idx"])
+
+
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_pass3_on_reference_indices(name):
+    meta, (Q, K, V), g = load_case(name)
+    B, H, k = meta["B"], meta["H"], meta["k"]
+    idx = torch.from_numpy(g["idx"].reshape(B, H, k)).to(DEV)
+    O = _api().fused_topk_attention(Q.to(DEV), K.to(DEV), V.to(DEV), idx)
+    assert O.dtype == Q.dtype and O.shape == (B, H, 64)
+    ok, st = attention_close(O.float().cpu().numpy(), g["O_f32"], got_rounded_to=dtype_name(Q))
+    assert ok, st
+
+
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_full_pipeline_vs_reference(oracle_mod, name):
+    meta, (Q, K, V), g = load_case(name)
+    B, H, k = meta["B"], meta["H"], meta["k"]
+    Qd, Kd, Vd = Q.to(DEV), K.to(DEV), V.to(DEV)
+    idx = _api().topk_qaxis_select(Qd, Kd, k).cpu().numpy().reshape(B * H, k)
+    _, _, idx_oracle, O_oracle = oracle_mod.decode(to_np(Q), to_np(K), to_np(V), dtype_name(Q), k)
+    assert np.array_equal(idx, idx_oracle), "indices differ from the oracle"
+    assert np.array_equal(idx, g["idx"]), "indices differ from the reference's"
+    O = _api().topk_qaxis_attention(Qd, Kd, Vd, k).float().cpu().numpy()
+    ok, st = attention_close(O, g["O_f32"], got_rounded_to=dtype_name(Q))
+    assert ok, st
+    if dtype_name(Q) == "bf16":  # the reference's own bf16 output: same bits almost always
+        ref = bf16_bits_to_f32(g["O_ref"])
+        assert np.mean(O == ref) >= 0.99
+        assert np.all(np.abs(O - ref) <= np.spacing(np.abs(ref)) * 2 ** 16 + 1e-30)
+
+
+# ---------------------------------------------------------------------------------------
+# Shapes, dtypes and edge cases against the oracle
+# ---------------------------------------------------------------------------------------
+DT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+SWEEP = [
+    # B, H, H_kv, N, k, dtype
+    (1, 4, 4, 2, 1, "bf16"),
+    (1, 8, 2, 9, 3, "bf16"),
+    (1, 8, 8, 64, 63, "f16"),
+    (3, 32, 8, 257, 100, "bf16"),
+    (2, 16, 2, 513, 256, "f16"),
+    (1, 32, 8, 1023, 511, "f32"),
+    (2, 8, 1, 5000, 2500, "bf16"),
+    (8, 32, 8, 5000, 2500, "bf16"),      # reference test_edge_case_b8_production
+    (1, 32, 8, 20000, 10000, "bf16"),    # reference test_fp32_softmax_state_long_context
+    (1, 32, 8, 20000, 1, "f16"),
+    (2, 64, 8, 3000, 450, "bf16"),       # G = 8
+    (1, 32, 8, 4096, 614, "f32"),        # config 0
+]
+
+
+def _check_vs_oracle(oracle_mod, Q, K, V, k, dt):
+    Qd, Kd, Vd = Q.to(DEV), K.to(DEV), V.to(DEV)
+    B, H = Q.shape[:2]
+    idx = _api().topk_qaxis_select(Qd, Kd, k).cpu().numpy().reshape(B * H, k)
+    O = _api().topk_qaxis_attention(Qd, Kd, Vd, k).float().cpu().numpy()
+    _, _, idx_o, O_o = oracle_mod.decode(to_np(Q), to_np(K), to_np(V), dt, k)
+    assert np.array_equal(idx, idx_o)
+    ok, st = attention_close(O, O_o, got_rounded_to=dt)
+    assert ok, st
+
+
+@pytest.mark.parametrize("B,H,H_kv,N,k,dt", SWEEP)
+def test_sweep_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=DT[dt], seed=N + k)
+    _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
+
+
+def test_strided_cache_view_matches_contiguous(oracle_mod):
+    """A cache allocated for N_max positions is used through a view, without a copy."""
+    from dcr_b200.synthetic import make_decode_inputs
+    B, H, H_kv, N, k = 2, 32, 8, 3000, 450
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=9)
+    Kb = torch.zeros(B, H_kv, N + 40, 64, dtype=K.dtype, device=DEV)
+    Vb = torch.zeros_like(Kb)
+    Kb[:, :, :N] = K.to(DEV)
+    Vb[:, :, :N] = V.to(DEV)
+    Kv, Vv = Kb[:, :, :N], Vb[:, :, :N]
+    assert not Kv.is_contiguous()
+    O1 = _api().topk_qaxis_attention(Q.to(DEV), Kv, Vv, k)
+    O2 = _api().topk_qaxis_attention(Q.to(DEV), K.to(DEV), V.to(DEV), k)
+    assert torch.equal(O1, O2)
+
+
+def test_side_stream_and_determinism():
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(4, 32, 8, 8192, dtype=torch.float16, seed=3, device=DEV)
+    O1 = _api().topk_qaxis_attention(Q, K, V, 1229)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        O2 = _api().topk_qaxis_attention(Q, K, V, 1229)
+    s.synchronize()
+    assert torch.equal(O1, O2)
+
+
+def test_cuda_graph_capture_replay():
+    from dcr_b200.kernel.cuda._common import workspace_bytes
+    from dcr_b200.synthetic import make_decode_inputs
+    B, H, H_kv, N, k = 4, 32, 8, 8192, 1229
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=4, device=DEV)
+    ws = torch.empty(workspace_bytes(B, H, H_kv, N, k), dtype=torch.uint8, device=DEV)
+    out = torch.empty(B, H, 64, dtype=Q.dtype, device=DEV)
+    want = _api().topk_qaxis_attention(Q, K, V, k)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _api().topk_qaxis_attention(Q, K, V, k, out=out, workspace_buf=ws)  # warm-up
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        _api().topk_qaxis_attention(Q, K, V, k, out=out, workspace_buf=ws)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    Q.copy_(torch.randn_like(Q))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, _api().topk_qaxis_attention(Q, K, V, k))
+    del g
+
+
+def test_out_of_range_indices_are_skipped_and_reported():
+    """Pass 3 checks every index against [0, N): a bad one is skipped (zero row) and
+    raises DCR_ERR_DEVICE_INDEX instead of reading outside the cache."""
+    from dcr_b200 import _lib
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(1, 8, 2, 256, dtype=torch.bfloat16, seed=1, device=DEV)
+    idx = torch.arange(0, 64, dtype=torch.int32, device=DEV).repeat(1, 8, 1).contiguous()
+    idx[0, 3, 5] = 256 + 7
+    idx[0, 4, 9] = -3
+    O = _api().fused_topk_attention(Q, K, V, idx)
+    st = _lib.read_device_status(clear=True)
+    assert st & _lib.DCR_ERR_DEVICE_INDEX
+    assert torch.isfinite(O.float()).all()
+
+
+def test_errors_mirror_reference():
+    from dcr_b200.kernel.cuda._common import KEffRangeError
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(1, 4, 2, 16, dtype=torch.bfloat16, seed=1, device=DEV)
+    with pytest.raises(ValueError, match="caller must dispatch to SDPA"):
+        _api().topk_qaxis_attention(Q, K, V, 16)
+    with pytest.raises(AssertionError):
+        _api().topk_qaxis_attention(Q, K, V, 0)
+    with pytest.raises(KEffRangeError):
+        _api().topk_pass2_select(torch.zeros(1, 4, 16, dtype=torch.bfloat16, device=DEV), 20)
+    with pytest.raises(AssertionError):
+        _api().topk_qaxis_attention(Q, K.float(), V, 4)
+    with pytest.raises(RuntimeError):
+        _api().topk_qaxis_attention(Q.cpu(), K.cpu(), V.cpu(), 4)
+
+
+# ---------------------------------------------------------------------------------------
+# Full size: BASELINE config 1 (hero), config 3 corners, one GPU's shard of config 4
+# ---------------------------------------------------------------------------------------
+def _topk_properties(scores: torch.Tensor, idx: torch.Tensor, k: int) -> None:
+    """Exact top-K with lower-index tie-break, checked without a sort."""
+    R, N = scores.shape
+    s = scores.float()
+    ix = idx.long()
+    assert ix.shape == (R, k)
+    assert bool((ix[:, 1:] > ix[:, :-1]).all()), "not strictly ascending"
+    assert int(ix.min()) >= 0 and int(ix.max()) < N
+    mask = torch.zeros(R, N, dtype=torch.bool, device=s.device)
+    mask.scatter_(1, ix, True)
+    assert bool((mask.sum(1) == k).all())
+    sel_min = torch.where(mask, s, torch.full_like(s, float("inf"))).min(1).values
+    uns_max = torch.where(~mask, s, torch.full_like(s, float("-inf"))).max(1).values
+    assert bool((sel_min >= uns_max).all()), "an unselected score beats a selected one"
+    pos = torch.arange(N, device=s.device).expand(R, N)
+    tie = s == sel_min[:, None]
+    last_sel_tie = torch.where(tie & mask, pos, torch.full_like(pos, -1)).max(1).values
+    first_uns_tie = torch.where(tie & ~mask, pos, torch.full_like(pos, N)).min(1).values
+    assert bool((last_sel_tie < first_uns_tie).all()), "ties not broken by lower index"
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("B,H,H_kv,N,c,dt", [
+    (4, 32, 8, 32768, 0.15, "f16"),      # config 1 (hero)
+    (4, 32, 8, 32768, 0.15, "bf16"),
+    (16, 32, 8, 8192, 0.30, "f16"),      # config 3 corners
+    (1, 32, 8, 131072, 0.05, "f16"),
+    (8, 4, 1, 262144, 0.05, "bf16"),     # config 4: one GPU of the 8-way KV-head split
+])
+def test_full_size_vs_oracle(oracle_mod, B, H, H_kv, N, c, dt):
+    from dcr_b200.models.llama.adaptive import adaptive_k_window
+    from dcr_b200.synthetic import make_decode_inputs
+    k = adaptive_k_window(64, N, c)
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=DT[dt], seed=0, device=DEV)
+    api = _api()
+    u = api.compute_u_Q(Q)
+    scores = api.topk_pass1_projection(K, u)
+    idx = api.topk_qaxis_select(Q, K, k)
+    _topk_properties(scores.reshape(B * H, N), idx.reshape(B * H, k), k)
+    O = api.topk_qaxis_attention(Q, K, V, k).float().cpu().numpy()
+    _, s_o, idx_o, O_o = oracle_mod.decode(to_np(Q), to_np(K), to_np(V), dt, k)
+    assert np.array_equal(to_np(scores).reshape(B * H, N), s_o)
+    assert np.array_equal(idx.cpu().numpy().reshape(B * H, k), idx_o)
+    ok, st = attention_close(O, O_o, got_rounded_to=dt)
+    assert ok, st
