@@ -220,7 +220,7 @@ def run_gpu_arm(args):
 
     B, H, H_kv, N, D = CFG["B"], CFG["H"], CFG["H_kv"], CFG["N"], CFG["D"]
     k = _k_eff(N, CFG["coverage"])
-    dt = torch.float16
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
     dcode = _lib.DTYPE_CODES[dt]
     eb = 2
     steps, warm = args.steps, args.warmup
@@ -247,27 +247,19 @@ def run_gpu_arm(args):
         if st:
             raise _lib.DCRError(st, "dcr_decode")
 
-    # separate buffers for the instrumented per-pass loop
+    # per-pass events recorded by dcr_decode_timed (same kernels as dcr_decode)
+    import ctypes
     rows = B * H
-    n_pad = (N + 7) // 8 * 8
-    scores = torch.empty(rows, n_pad, dtype=torch.bfloat16, device=dev)
     idx = torch.empty(rows, k, dtype=torch.int32, device=dev)
 
     def step_instrumented(i, ev):
         K, V = caches[i % LAYERS]
-        q = Qs[i % Qs.shape[0]]
-        ev[0].record(stream)
-        st = lib.dcr_score(K.data_ptr(), dcode, ksb, ksh, None, q.data_ptr(), 1e-12, B, H, H_kv,
-                           N, D, scores.data_ptr(), n_pad, sp)
-        ev[1].record(stream)
-        st |= lib.dcr_select(scores.data_ptr(), n_pad, rows, N, k, idx.data_ptr(), sp)
-        ev[2].record(stream)
-        st |= lib.dcr_attend(q.data_ptr(), K.data_ptr(), V.data_ptr(), dcode, ksb, ksh, ksb, ksh,
-                             idx.data_ptr(), B, H, H_kv, N, D, k, O.data_ptr(), ws.data_ptr(),
-                             ws_n, sp)
-        ev[3].record(stream)
+        arr = (ctypes.c_void_p * 4)(*[e.cuda_event for e in ev])
+        st = lib.dcr_decode_timed(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), V.data_ptr(),
+                                  dcode, ksb, ksh, ksb, ksh, B, H, H_kv, N, D, k, 1e-12,
+                                  O.data_ptr(), ws.data_ptr(), ws_n, sp, arr)
         if st:
-            raise _lib.DCRError(st, "per-pass step")
+            raise _lib.DCRError(st, "dcr_decode_timed")
 
     def barrier():
         if world > 1:
@@ -307,6 +299,9 @@ def run_gpu_arm(args):
 
     # ---- instrumented loop: per-kernel CUDA events (same stream) -----------------------
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for e in evs:
+        for x in e:
+            x.record(stream)  # materialise the CUDA events
     barrier()
     for i in range(steps):
         step_instrumented(i, evs[i])
@@ -377,7 +372,7 @@ def run_gpu_arm(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        per_layer, threads, n, bs = cpu_reference_time(B, H, H_kv, N, k, CFG["dtype"], 0,
+        per_layer, threads, n, bs = cpu_reference_time(B, H, H_kv, N, k, args.dtype, 0,
                                                        budget_s=args.cpu_budget)
         cpu = {"value": round(per_layer * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"C oracle (oracle/dcr_oracle.c, OpenMP, restating the reference's "
@@ -389,7 +384,7 @@ def run_gpu_arm(args):
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 5),
-        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype,
         "data": "synthetic",
         "config": {"workload": "config1 hero single-layer decode (fresh Q per step)",
                    "B_per_rank": B, "N": N, "H": H, "H_kv": H_kv, "D": D, "k_eff": k,
@@ -430,6 +425,8 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5, help="untimed seconds before timing")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default=CFG["dtype"],
+                    help="cache/query dtype (config 1 is fp16)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

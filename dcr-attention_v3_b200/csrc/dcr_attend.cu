@@ -13,9 +13,13 @@
 // head j of KV group (b, h_kv); the G heads of one group and piece are launched next to
 // each other, so the rows they share are fetched from HBM once and served from L2.
 // Each CTA gathers 64-row tiles of K and V with 16-byte cp.async copies (8 lanes per
-// 128-byte row, fully coalesced) into a 4-stage ring of 128-byte-swizzled shared-memory
-// tiles. Scores use two threads per row (32 dims each, Q held in registers); the P.V
-// product uses one thread per (dimension pair, 16-row group). Each CTA writes its partial
+// 128-byte row, fully coalesced) into a 3-stage ring of 128-byte-swizzled shared-memory
+// tiles (4 CTAs per SM); the indices of a tile are loaded two iterations before its
+// copies are issued.
+// Warp w owns rows 16w..16w+15 of every tile and keeps its own online-softmax state:
+// scores use two lanes per row (32 dims each, Q held in registers) and the P.V product
+// one lane per dimension pair, so a tile needs no block barrier besides the stage
+// hand-over. The 4 warp states are merged at the end. Each CTA writes its partial
 // (m, l, o[64]) to the workspace; the last CTA of a (b, h) to finish (atomic ticket,
 // no waiting) merges the S partials:
 //     M = max_s m_s,  O = sum_s e^{m_s - M} o_s / sum_s e^{m_s - M} l_s.
@@ -37,7 +41,8 @@ struct P3Cfg {
   static constexpr int kChunks = RowTraits<T>::kChunks;
   static constexpr int kTileBytes = kP3Tile * kRowBytes;  // one of K or V
   static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStages = sizeof(T) == 4 ? 3 : 4;
+  static constexpr int kStages = 3;
+  static constexpr int kMinBlocks = sizeof(T) == 4 ? 2 : 4;  // CTAs per SM
   static constexpr int kSmem = 1024 + kStages * kStageBytes;
 };
 
@@ -54,21 +59,22 @@ struct P3Params {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p) {
+__global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kernel(const P3Params p) {
   using Cfg = P3Cfg<T>;
   constexpr int kChunks = Cfg::kChunks;
   constexpr int kPer = ElemTraits<T>::kPerChunk;
   constexpr int kHalfChunks = kChunks / 2;
   constexpr int kRowsPerPass = kP3Threads / kChunks;  // 16 (16-bit) or 8 (fp32)
   constexpr int kPasses = kP3Tile / kRowsPerPass;     // 4 or 8
+  constexpr int kWarps = kP3Threads / 32;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   __shared__ float P_s[kP3Tile];
-  __shared__ float red[kP3Threads / 32];
-  __shared__ float o_red[kP3Threads / 32][kD];
-  __shared__ float l_red[kP3Threads / 32];
+  __shared__ float o_red[kWarps][kD];
+  __shared__ float m_red[kWarps];
+  __shared__ float l_red[kWarps];
   __shared__ int is_last;
 
   const int tid = threadIdx.x;
@@ -92,8 +98,8 @@ __global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p)
   const uint8_t* kbase = static_cast<const uint8_t*>(p.k) + (b * p.ksb + hk * p.ksh) * static_cast<int64_t>(sizeof(T));
   const uint8_t* vbase = static_cast<const uint8_t*>(p.v) + (b * p.vsb + hk * p.vsh) * static_cast<int64_t>(sizeof(T));
 
-  // Q half owned by this thread (two threads per row in the score phase).
-  const int half = tid & 1;
+  // Q half owned by this thread (two lanes per row in the score phase).
+  const int half = lane & 1;
   float qf[kD / 2];
   {
     const uint8_t* qrow = static_cast<const uint8_t*>(p.q) + row * kD * static_cast<int64_t>(sizeof(T));
@@ -107,59 +113,80 @@ __global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p)
     }
   }
 
-  auto issue = [&](int tt) {
+  // Gather assignment: thread copies chunk `cchunk` of rows rbase + i * kRowsPerPass.
+  const int cchunk = tid % kChunks;
+  const int rbase = tid / kChunks;
+
+  // Indices of the rows this thread copies in tile tt (-1: past the end of the list).
+  auto load_idx = [&](int tt, int32_t (&n)[kPasses]) {
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+      const int pos = tt * kP3Tile + rbase + i * kRowsPerPass;
+      n[i] = (pos < cnt) ? __ldg(idx_row + pos) : -1;
+    }
+  };
+  auto issue = [&](int tt, const int32_t (&n)[kPasses]) {
     if (tt < ntiles) {
       uint8_t* kt = smem + (tt % Cfg::kStages) * Cfg::kStageBytes;
       uint8_t* vt = kt + Cfg::kTileBytes;
-      const int c = tid % kChunks;
 #pragma unroll
       for (int i = 0; i < kPasses; ++i) {
-        const int r = tid / kChunks + i * kRowsPerPass;
-        const int pos = tt * kP3Tile + r;
-        uint32_t bytes = 0;
-        int64_t n = 0;
-        if (pos < cnt) {
-          n = idx_row[pos];
-          if (n >= 0 && n < p.N) {
-            bytes = 16;
-          } else {
-            if (c == 0) raise_status(DCR_ERR_DEVICE_INDEX);
-            n = 0;
+        const int r = rbase + i * kRowsPerPass;
+        int64_t nn = n[i];
+        uint32_t bytes = 16;
+        if (nn < 0 || nn >= p.N) {
+          if (nn >= 0 || tt * kP3Tile + r < cnt) {
+            if (cchunk == 0) raise_status(DCR_ERR_DEVICE_INDEX);
           }
+          nn = 0;
+          bytes = 0;  // zero-fill, read nothing
         }
-        const uint32_t off = swz_offset(r, c, kP3Tile);
-        cp_async_16(kt + off, kbase + n * Cfg::kRowBytes + c * 16, bytes);
-        cp_async_16(vt + off, vbase + n * Cfg::kRowBytes + c * 16, bytes);
+        const uint32_t off = swz_offset(r, cchunk, kP3Tile);
+        cp_async_16(kt + off, kbase + nn * Cfg::kRowBytes + cchunk * 16, bytes);
+        cp_async_16(vt + off, vbase + nn * Cfg::kRowBytes + cchunk * 16, bytes);
       }
     }
     cp_async_commit();  // always commit so group counting stays uniform
   };
 
+  {
+    int32_t n0[kPasses];
 #pragma unroll
-  for (int i = 0; i < Cfg::kStages - 1; ++i) issue(i);
+    for (int i = 0; i < Cfg::kStages - 1; ++i) {
+      load_idx(i, n0);
+      issue(i, n0);
+    }
+  }
+  // Index prefetch two iterations deep: n_next is issued this iteration, n_after next.
+  int32_t n_next[kPasses], n_after[kPasses];
+  load_idx(Cfg::kStages - 1, n_next);
+  load_idx(Cfg::kStages, n_after);
 
-  float m_run = -INFINITY;
-  float l_part = 0.0f;
-  float o0 = 0.0f, o1 = 0.0f;
-  const int dp = lane;  // dimension pair 2dp, 2dp+1
-  const int rg = warp;  // rows rg*16 .. rg*16+15 in the P.V phase
+  // Per-warp online-softmax state: warp w owns rows 16w .. 16w+15 of every tile.
+  float m_w = -INFINITY;
+  float l_part = 0.0f;       // lanes with half == 0 accumulate their row's weights
+  float o0 = 0.0f, o1 = 0.0f;  // dims 2*lane, 2*lane+1
+  const int r_own = warp * 16 + (lane >> 1);
 
   for (int tt = 0; tt < ntiles; ++tt) {
     cp_async_wait<Cfg::kStages - 2>();
-    __syncthreads();
-    issue(tt + Cfg::kStages - 1);
+    __syncthreads();  // tile tt visible to all; stage (tt-1) free for reuse
+    issue(tt + Cfg::kStages - 1, n_next);
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) n_next[i] = n_after[i];
+    load_idx(tt + Cfg::kStages + 1, n_after);
 
     const uint8_t* kt = smem + (tt % Cfg::kStages) * Cfg::kStageBytes;
     const uint8_t* vt = kt + Cfg::kTileBytes;
     const uint32_t kt_addr = smem_u32(kt);
+    const uint32_t vt_addr = smem_u32(vt);
 
-    // ---- scores: row r = tid / 2, dims [32*half, 32*half + 32) ----
-    const int r = tid >> 1;
+    // ---- scores of the warp's 16 rows: dims [32*half, 32*half + 32) per lane ----
     float acc0 = 0.0f, acc1 = 0.0f;
 #pragma unroll
     for (int c = 0; c < kHalfChunks; ++c) {
       float f[kPer];
-      ElemTraits<T>::widen(lds128(kt_addr + swz_offset(r, half * kHalfChunks + c, kP3Tile)), f);
+      ElemTraits<T>::widen(lds128(kt_addr + swz_offset(r_own, half * kHalfChunks + c, kP3Tile)), f);
 #pragma unroll
       for (int e = 0; e < kPer; e += 2) {
         acc0 = fmaf(f[e], qf[c * kPer + e], acc0);
@@ -169,39 +196,33 @@ __global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p)
     float z = acc0 + acc1;
     z += __shfl_xor_sync(0xffffffffu, z, 1);
     z *= 0.125f;  // 1 / sqrt(64), exact
-    const bool valid = tt * kP3Tile + r < cnt;
-    if (!valid) z = -INFINITY;
-
-    float mt = z;
+    const bool valid = tt * kP3Tile + r_own < cnt;
+    float mt = valid ? z : -INFINITY;
 #pragma unroll
     for (int off = 2; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-    if (lane == 0) red[warp] = mt;
-    __syncthreads();
-    const float m_tile = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    const float m_new = fmaxf(m_run, m_tile);
-    const float alpha = expf(m_run - m_new);
+    const float m_new = fmaxf(m_w, mt);
+    const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_w - m_new);
     const float pr = valid ? expf(z - m_new) : 0.0f;
-    if (half == 0) P_s[r] = pr;
+    if (half == 0) P_s[r_own] = pr;
     l_part = l_part * alpha + (half == 0 ? pr : 0.0f);
-    m_run = m_new;
-    __syncthreads();
+    m_w = m_new;
+    __syncwarp();
 
-    // ---- P.V: thread (dp, rg) accumulates dims 2dp, 2dp+1 over 16 rows ----
+    // ---- P.V over the warp's rows: lane owns dims 2*lane, 2*lane+1 ----
     o0 *= alpha;
     o1 *= alpha;
-    const uint32_t vt_addr = smem_u32(vt);
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const int rr = rg * 16 + i;
+      const int rr = warp * 16 + i;
       const float pw = P_s[rr];
       if constexpr (sizeof(T) == 4) {
-        const uint32_t addr = vt_addr + swz_offset(rr, dp >> 1, kP3Tile) + (dp & 1) * 8;
+        const uint32_t addr = vt_addr + swz_offset(rr, lane >> 1, kP3Tile) + (lane & 1) * 8;
         float2 v2;
         asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v2.x), "=f"(v2.y) : "r"(addr));
         o0 = fmaf(pw, v2.x, o0);
         o1 = fmaf(pw, v2.y, o1);
       } else {
-        const uint32_t addr = vt_addr + swz_offset(rr, dp >> 2, kP3Tile) + (dp & 3) * 4;
+        const uint32_t addr = vt_addr + swz_offset(rr, lane >> 2, kP3Tile) + (lane & 3) * 4;
         uint32_t w;
         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(addr));
         const float2 v2 = ElemTraits<T>::widen2(w);
@@ -212,28 +233,42 @@ __global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p)
   }
   cp_async_wait<0>();
 
-  // ---- CTA reduction: l over threads, o over the 4 row groups ----
+  // ---- merge the 4 warps' (m, l, o) ----
   float ls = l_part;
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
-  if (lane == 0) l_red[warp] = ls;
-  o_red[rg][2 * dp] = o0;
-  o_red[rg][2 * dp + 1] = o1;
+  if (lane == 0) {
+    m_red[warp] = m_w;
+    l_red[warp] = ls;
+  }
+  o_red[warp][2 * lane] = o0;
+  o_red[warp][2 * lane + 1] = o1;
   __syncthreads();
-  const float l_cta = (l_red[0] + l_red[1]) + (l_red[2] + l_red[3]);
+  float M = m_red[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) M = fmaxf(M, m_red[w]);
+  float sc[kWarps];
+  float l_cta = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    sc[w] = (m_red[w] == -INFINITY) ? 0.0f : expf(m_red[w] - M);
+    l_cta = fmaf(sc[w], l_red[w], l_cta);
+  }
+  float od = 0.0f;
+  if (tid < kD) {
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) od = fmaf(sc[w], o_red[w][tid], od);
+  }
 
   if (p.S == 1) {
-    if (tid < kD) {
-      const float od = (o_red[0][tid] + o_red[1][tid]) + (o_red[2][tid] + o_red[3][tid]);
-      ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / l_cta);
-    }
+    if (tid < kD) ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / l_cta);
     return;
   }
 
   float* mine = p.part + (row * p.S + s) * (kD + 2);
-  if (tid < kD) mine[2 + tid] = (o_red[0][tid] + o_red[1][tid]) + (o_red[2][tid] + o_red[3][tid]);
+  if (tid < kD) mine[2 + tid] = od;
   if (tid == 0) {
-    mine[0] = m_run;
+    mine[0] = M;
     mine[1] = l_cta;
   }
   __threadfence();
@@ -244,22 +279,23 @@ __global__ void __launch_bounds__(kP3Threads, 3) attend_kernel(const P3Params p)
   __threadfence();
   if (tid < kD) {
     const float* base = p.part + row * p.S * (kD + 2);
-    float M = -INFINITY;
-    for (int t = 0; t < p.S; ++t) M = fmaxf(M, __ldcg(base + t * (kD + 2)));
-    float L = 0.0f, od = 0.0f;
+    float Mg = -INFINITY;
+    for (int t = 0; t < p.S; ++t) Mg = fmaxf(Mg, __ldcg(base + t * (kD + 2)));
+    float L = 0.0f, o = 0.0f;
     for (int t = 0; t < p.S; ++t) {
       const float* pt = base + t * (kD + 2);
-      const float w = expf(__ldcg(pt) - M);
+      const float mt = __ldcg(pt);
+      const float w = (mt == -INFINITY) ? 0.0f : expf(mt - Mg);
       L = fmaf(w, __ldcg(pt + 1), L);
-      od = fmaf(w, __ldcg(pt + 2 + tid), od);
+      o = fmaf(w, __ldcg(pt + 2 + tid), o);
     }
-    ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / L);
+    ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), o / L);
   }
   if (tid == 0) p.counters[row] = 0;
 }
 
 int attend_splits(int rows, int k_eff) {
-  const int slots = device_sm_count() * 3;  // 3 CTAs per SM
+  const int slots = device_sm_count() * 4;  // 4 CTAs per SM (16-bit caches)
   int S = slots / (rows > 0 ? rows : 1);
   const int max_by_tiles = (k_eff + kP3Tile - 1) / kP3Tile;
   if (S > max_by_tiles) S = max_by_tiles;

@@ -175,7 +175,7 @@ int dcr_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h, 
   if (u == nullptr && !aligned16(Q)) return DCR_ERR_ALIGN;
   if (s_stride_row < N) return DCR_ERR_SHAPE;
   return launch_score(K, dtype, k_stride_b, k_stride_h, u, Q, eps, B, H, H_kv, N, scores,
-                      s_stride_row, static_cast<cudaStream_t>(stream));
+                      s_stride_row, 0, static_cast<cudaStream_t>(stream));
 }
 
 int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
@@ -184,7 +184,7 @@ int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, in
   if (rows <= 0 || N <= 0 || s_stride_row < N) return DCR_ERR_SHAPE;
   int st = check_k(k_eff, N);
   if (st) return st;
-  return launch_select(scores, s_stride_row, rows, N, k_eff, idx_out, nullptr,
+  return launch_select(scores, s_stride_row, rows, N, k_eff, 0, idx_out, nullptr,
                        static_cast<cudaStream_t>(stream));
 }
 
@@ -232,15 +232,16 @@ int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride
   uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
-                         w.n_pad, s)))
+                         w.n_pad, 1, s)))
     return st;
-  return launch_select(scores, w.n_pad, rows, N, k_eff, idx_out, nullptr, s);
+  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
 }
 
-int dcr_decode(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
-               int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, int B, int H,
-               int H_kv, int N, int D, int k_eff, float eps, void* O, void* workspace,
-               size_t workspace_bytes, void* stream) {
+static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
+                       int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                       int64_t v_stride_h, int B, int H, int H_kv, int N, int D, int k_eff,
+                       float eps, void* O, void* workspace, size_t workspace_bytes,
+                       void* stream, void* const* events) {
   int st = check_heads(B, H, H_kv, N, D);
   if (st) return st;
   if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
@@ -257,13 +258,43 @@ int dcr_decode(const void* Q, const void* K, const void* V, int dtype, int64_t k
   int* counters = reinterpret_cast<int*>(ws + w.counters);
   float* partials = reinterpret_cast<float*>(ws + w.partials);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto mark = [&](int i) -> int {
+    if (events == nullptr) return DCR_OK;
+    return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess ? DCR_OK
+                                                                                 : DCR_ERR_CUDA;
+  };
+  if ((st = mark(0))) return st;
+  // Pass 1 stores order keys, which Pass 2 reads directly.
   if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
-                         w.n_pad, s)))
+                         w.n_pad, 1, s)))
     return st;
+  if ((st = mark(1))) return st;
   // Pass 2 also resets the Pass 3 split-K tickets of its row.
-  if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, idx, counters, s))) return st;
-  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B, H,
-                       H_kv, N, k_eff, O, w.splits, partials, counters, s);
+  if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s))) return st;
+  if ((st = mark(2))) return st;
+  if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B,
+                          H, H_kv, N, k_eff, O, w.splits, partials, counters, s)))
+    return st;
+  return mark(3);
+}
+
+int dcr_decode(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+               int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, int B, int H,
+               int H_kv, int N, int D, int k_eff, float eps, void* O, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
+                     N, D, k_eff, eps, O, workspace, workspace_bytes, stream, nullptr);
+}
+
+int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+                     int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, int B, int H,
+                     int H_kv, int N, int D, int k_eff, float eps, void* O, void* workspace,
+                     size_t workspace_bytes, void* stream, void* const* events) {
+  if (events == nullptr) return DCR_ERR_NULL;
+  for (int i = 0; i < 4; ++i)
+    if (events[i] == nullptr) return DCR_ERR_NULL;
+  return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
+                     N, D, k_eff, eps, O, workspace, workspace_bytes, stream, events);
 }
 
 int dcr_read_device_status(int* status_out, int clear) {

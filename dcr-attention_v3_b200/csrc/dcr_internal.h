@@ -34,12 +34,14 @@ WorkspaceLayout workspace_layout(int rows, int N, int k_eff);
 
 int launch_unit_query(const void* Q, int dtype, int rows, float eps, float* u, cudaStream_t st);
 
+// keys_out != 0: store 16-bit order keys (bf16_order_key) instead of bf16 score bits.
 int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
                  const float* u, const void* Q, float eps, int B, int H, int H_kv, int N,
-                 uint16_t* scores, int64_t s_stride_row, cudaStream_t st);
+                 uint16_t* scores, int64_t s_stride_row, int keys_out, cudaStream_t st);
 
+// keys_in != 0: the rows hold order keys (from launch_score with keys_out) not bf16 bits.
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
-                  int32_t* idx, int* row_counters, cudaStream_t st);
+                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st);
 
 int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
                   int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,

@@ -9,12 +9,18 @@
 //
 // Design (B200): the pass is a pure HBM stream of the K cache (128 B per row for 16-bit
 // caches) with G = H / H_kv query heads scored per row. A persistent grid of
-// 2 CTAs per SM walks contiguous ranges of row tiles; one thread per CTA issues 4-D TMA
-// tile loads (128-byte swizzle) into a 3-stage shared-memory ring completed by
-// mbarriers, and every thread scores RPT rows of each tile against the G unit queries of
-// the tile's (b, h_kv) group. The fp32 dot product of every (row, head) runs
-// d = 0..63 as one chain of fused multiply-adds from 0, so a CPU restatement with
-// fmaf in the same order reproduces every score bit for bit.
+// 2 CTAs per SM walks contiguous ranges of 256-row tiles; one thread per CTA issues 4-D
+// TMA tile loads (128-byte swizzle) into a 3-stage shared-memory ring completed by
+// mbarriers. Every thread scores two rows of each tile (r and r + 128) with packed fp32
+// FMAs (fma.rn.f32x2) that advance two heads of one row per instruction: the unit
+// queries sit in shared memory transposed, u_t[d][head], so one 16-byte load feeds two
+// head pairs. (For G = 1 the pair is two rows of one head and u is stored as {u, u}.)
+// Each lane of the packed FMA is an IEEE fma, so the fp32 dot product of every
+// (row, head) is still one chain of fused multiply-adds over d = 0..63 from 0, and a CPU
+// restatement with fmaf in that order reproduces every score bit for bit.
+// A tile's scores are staged in shared memory and written out during the next tile with
+// one 16-byte store per thread. The fused decode path stores the 16-bit order keys of
+// the scores (see bf16_order_key) instead of their bf16 bits, so Pass 2 reads keys.
 //
 // The unit query is computed by one warp per query row: lane l squares elements 2l and
 // 2l+1 (x0*x0 rounded, then fmaf(x1, x1, .)), the 32 partial sums are combined by an
@@ -47,9 +53,11 @@ __device__ __forceinline__ void load_pair(const void* row, int lane, float& x0, 
   }
 }
 
-// One warp: u_row[0..63] = q_row / max(||q_row||, eps). All lanes of the warp must call.
+// One warp: u[d] = q_row[d] / max(||q_row||, eps) for d = 0..63, written as
+// u_out[d * stride]. All lanes of the warp must call.
 template <typename T>
-__device__ __forceinline__ void unit_query_warp(const void* q_row, float eps, float* u_row) {
+__device__ __forceinline__ void unit_query_warp(const void* q_row, float eps, float* u_out,
+                                                int stride = 1) {
   const int lane = threadIdx.x & 31;
   float x0, x1;
   load_pair<T>(q_row, lane, x0, x1);
@@ -58,8 +66,8 @@ __device__ __forceinline__ void unit_query_warp(const void* q_row, float eps, fl
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, off);
   const float norm = fmaxf(sqrtf(part), eps);
-  u_row[2 * lane] = x0 / norm;
-  u_row[2 * lane + 1] = x1 / norm;
+  u_out[(2 * lane) * stride] = x0 / norm;
+  u_out[(2 * lane + 1) * stride] = x1 / norm;
 }
 
 template <typename T>
@@ -92,19 +100,41 @@ int launch_unit_query(const void* Q, int dtype, int rows, float eps, float* u, c
 // Pass 1
 // ---------------------------------------------------------------------------------------
 constexpr int kP1Threads = 128;
-constexpr int kP1Stages = 3;
 
 template <typename T>
 struct P1Cfg {
-  static constexpr int kRPT = (sizeof(T) == 4) ? 1 : 2;  // rows per thread per tile
-  static constexpr int kTileRows = kP1Threads * kRPT;   // 256 (16-bit) or 128 (fp32)
-  static constexpr int kStageBytes = kTileRows * RowTraits<T>::kRowBytes;  // 32 KiB
+  static constexpr int kRPT = 2;                        // rows per thread per tile
+  static constexpr int kTileRows = kP1Threads * kRPT;   // 256
+  static constexpr int kStageBytes = kTileRows * RowTraits<T>::kRowBytes;  // 32 / 64 KiB
+  static constexpr int kStages = sizeof(T) == 4 ? 2 : 3;
+  static constexpr int kCtasPerSm = sizeof(T) == 4 ? 1 : 2;
   static constexpr int kBoxCols = 128 / ElemTraits<T>::kBytes;            // 64 or 32
 };
 
+template <int G>
+__host__ __device__ constexpr int p1_u_bytes() {
+  return G == 1 ? kD * 8 : G * kD * 4;  // {u, u} pairs, or u_t[d][G]
+}
+
 template <typename T, int G>
-constexpr int p1_smem_bytes() {
-  return 1024 + kP1Stages * P1Cfg<T>::kStageBytes + G * kD * 4 + kP1Stages * 8;
+__host__ __device__ constexpr int p1_smem_bytes() {
+  // tiles + unit queries + double-buffered score staging [2][G][256] u16 + mbarriers
+  return 1024 + P1Cfg<T>::kStages * P1Cfg<T>::kStageBytes + p1_u_bytes<G>() +
+         2 * G * P1Cfg<T>::kTileRows * 2 + P1Cfg<T>::kStages * 8;
+}
+
+// Two IEEE fused multiply-adds in one instruction: {a.x*b.x + c.x, a.y*b.y + c.y}.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
 }
 
 struct P1Params {
@@ -113,6 +143,8 @@ struct P1Params {
   float eps;
   uint16_t* scores;
   int64_t s_stride;
+  int keys_out;    // store order keys instead of bf16 bits
+  int vec_store;   // score rows are 16-byte aligned (16-byte stores)
   int N;
   int H_kv;
   int tiles_per_group;
@@ -129,19 +161,21 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, ui
 }
 
 template <typename T, int G>
-__global__ void __launch_bounds__(kP1Threads, 2)
+__global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
     score_kernel(const __grid_constant__ CUtensorMap kmap, const P1Params p) {
   using Cfg = P1Cfg<T>;
   constexpr int kChunks = RowTraits<T>::kChunks;
   constexpr int kPer = ElemTraits<T>::kPerChunk;
-  constexpr int kRPT = Cfg::kRPT;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kTR = Cfg::kTileRows;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
-  float* u_s = reinterpret_cast<float*>(smem + kP1Stages * Cfg::kStageBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(u_s + G * kD);
+  float* u_s = reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes);
+  uint16_t* stage_sc = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(u_s) + p1_u_bytes<G>());
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_sc + 2 * G * kTR);
 
   const int tid = threadIdx.x;
   const int t_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_tiles / gridDim.x);
@@ -153,106 +187,187 @@ __global__ void __launch_bounds__(kP1Threads, 2)
   if (tid == 0) {
     tma_prefetch_desc(&kmap);
 #pragma unroll
-    for (int s = 0; s < kP1Stages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
   }
   __syncthreads();
 
-  auto issue = [&](int it) {
+  auto tile_of = [&](int it, int& g, int& n0) {
     const int t = t_begin + it;
-    const int s = it % kP1Stages;
-    const int g = t / p.tiles_per_group;
-    const int n0 = (t - g * p.tiles_per_group) * Cfg::kTileRows;
+    g = t / p.tiles_per_group;
+    n0 = (t - g * p.tiles_per_group) * kTR;
+  };
+  auto issue = [&](int it) {
+    int g, n0;
+    tile_of(it, g, n0);
+    const int s = it % kStages;
     const int b = g / p.H_kv;
     const int hk = g - b * p.H_kv;
     uint8_t* dst = tiles + s * Cfg::kStageBytes;
     mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
 #pragma unroll
     for (int sub = 0; sub < RowTraits<T>::kSubTiles; ++sub)
-      tma_load_4d(dst + sub * Cfg::kTileRows * 128, &kmap, &full[s], sub * Cfg::kBoxCols, n0, hk,
-                  b);
+      tma_load_4d(dst + sub * kTR * 128, &kmap, &full[s], sub * Cfg::kBoxCols, n0, hk, b);
+  };
+  // Writes the staged scores of tile `it` (buffer it & 1) to global memory: thread t
+  // stores 8 consecutive scores of one head row per pass.
+  auto flush = [&](int it) {
+    int g, n0;
+    tile_of(it, g, n0);
+    const uint16_t* src = stage_sc + (it & 1) * G * kTR;
+#pragma unroll
+    for (int i = tid; i < G * kTR / 8; i += kP1Threads) {
+      const int j = i / (kTR / 8);
+      const int r = (i - j * (kTR / 8)) * 8;
+      const int n = n0 + r;
+      uint16_t* dst = p.scores + (static_cast<int64_t>(g) * G + j) * p.s_stride + n;
+      const uint4 v = *reinterpret_cast<const uint4*>(src + j * kTR + r);
+      if (p.vec_store && n + 8 <= p.N) {
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (n + q < p.N) dst[q] = e[q];
+      }
+    }
   };
 
   if (tid == 0) {
-    const int pre = my_tiles < kP1Stages ? my_tiles : kP1Stages;
+    const int pre = my_tiles < kStages ? my_tiles : kStages;
     for (int it = 0; it < pre; ++it) issue(it);
   }
 
   int cur_group = -1;
   for (int it = 0; it < my_tiles; ++it) {
-    const int t = t_begin + it;
-    const int s = it % kP1Stages;
-    const int g = t / p.tiles_per_group;
-    const int n0 = (t - g * p.tiles_per_group) * Cfg::kTileRows;
+    int g, n0;
+    tile_of(it, g, n0);
+    const int s = it % kStages;
 
     if (g != cur_group) {  // uniform across the CTA
       __syncthreads();     // earlier readers of u_s are done
-      if (p.u != nullptr) {
-        for (int i = tid; i < G * kD; i += kP1Threads) u_s[i] = p.u[static_cast<size_t>(g) * G * kD + i];
-      } else {
-        const int warp = tid >> 5;
-        for (int j = warp; j < G; j += kP1Threads / 32) {
+      const int warp = tid >> 5;
+      for (int j = warp; j < G; j += kP1Threads / 32) {
+        if (p.u != nullptr) {
+          const float* src = p.u + (static_cast<size_t>(g) * G + j) * kD;
+          for (int d = tid & 31; d < kD; d += 32) {
+            if (G == 1) {
+              u_s[2 * d] = src[d];
+              u_s[2 * d + 1] = src[d];
+            } else {
+              u_s[d * G + j] = src[d];
+            }
+          }
+        } else {
           const char* q_row = static_cast<const char*>(p.q) +
                               (static_cast<size_t>(g) * G + j) * kD * sizeof(T);
-          unit_query_warp<T>(q_row, p.eps, u_s + j * kD);
+          if (G == 1) {
+            unit_query_warp<T>(q_row, p.eps, u_s, 2);
+            __syncwarp();
+            for (int d = tid & 31; d < kD; d += 32) u_s[2 * d + 1] = u_s[2 * d];
+          } else {
+            unit_query_warp<T>(q_row, p.eps, u_s + j, G);
+          }
         }
       }
       __syncthreads();
       cur_group = g;
     }
 
-    const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / kP1Stages) & 1));
+    if (it > 0) flush(it - 1);  // scores of the previous tile, staged before the barrier
+
+    const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / kStages) & 1));
 
     const uint32_t tile_addr = smem_u32(tiles + s * Cfg::kStageBytes);
-    float acc[kRPT][G];
-#pragma unroll
-    for (int rr = 0; rr < kRPT; ++rr)
-#pragma unroll
-      for (int j = 0; j < G; ++j) acc[rr][j] = 0.0f;
+    const int r0 = tid;
+    const int r1 = tid + kP1Threads;
+    float res[2][G];  // [row][head]
 
+    if constexpr (G == 1) {
+      // pair = (row r0, row r1) of the single head; u_s holds {u, u}
+      float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      float kf[kRPT][kPer];
+      for (int c = 0; c < kChunks; ++c) {
+        float f0[kPer], f1[kPer];
+        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r0, c, kTR)), f0);
+        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r1, c, kTR)), f1);
+        const float4* ud = reinterpret_cast<const float4*>(u_s + c * kPer * 2);
 #pragma unroll
-      for (int rr = 0; rr < kRPT; ++rr) {
-        const int r = tid + rr * kP1Threads;
-        const uint4 v = lds128(tile_addr + swz_offset(r, c, Cfg::kTileRows));
-        ElemTraits<T>::widen(v, kf[rr]);
-      }
-#pragma unroll
-      for (int j = 0; j < G; ++j) {
-        float uv[kPer];
-        const float4* u4 = reinterpret_cast<const float4*>(u_s + j * kD + c * kPer);
-#pragma unroll
-        for (int q4 = 0; q4 < kPer / 4; ++q4) {
-          const float4 t4 = u4[q4];
-          uv[4 * q4 + 0] = t4.x;
-          uv[4 * q4 + 1] = t4.y;
-          uv[4 * q4 + 2] = t4.z;
-          uv[4 * q4 + 3] = t4.w;
+        for (int q = 0; q < kPer / 2; ++q) {
+          const float4 t4 = ud[q];
+          acc = ffma2(make_float2(f0[2 * q], f1[2 * q]), make_float2(t4.x, t4.y), acc);
+          acc = ffma2(make_float2(f0[2 * q + 1], f1[2 * q + 1]), make_float2(t4.z, t4.w), acc);
         }
+      }
+      res[0][0] = acc.x;
+      res[1][0] = acc.y;
+    } else {
+      // pair = (head 2m, head 2m+1) of one row; u_s is u_t[d][G]
+      constexpr int kPairs = G / 2;
+      float2 acc[2][kPairs];
 #pragma unroll
-        for (int e = 0; e < kPer; ++e)
+      for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
-          for (int rr = 0; rr < kRPT; ++rr) acc[rr][j] = fmaf(kf[rr][e], uv[e], acc[rr][j]);
+        for (int m = 0; m < kPairs; ++m) acc[rr][m] = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int c = 0; c < kChunks; ++c) {
+        float f0[kPer], f1[kPer];
+        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r0, c, kTR)), f0);
+        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r1, c, kTR)), f1);
+#pragma unroll
+        for (int e = 0; e < kPer; ++e) {
+          const float* ud = u_s + (c * kPer + e) * G;
+          float uv[G];
+          if constexpr (G == 2) {
+            const float2 t2 = *reinterpret_cast<const float2*>(ud);
+            uv[0] = t2.x;
+            uv[1] = t2.y;
+          } else {
+#pragma unroll
+            for (int q4 = 0; q4 < G / 4; ++q4) {
+              const float4 t4 = reinterpret_cast<const float4*>(ud)[q4];
+              uv[4 * q4 + 0] = t4.x;
+              uv[4 * q4 + 1] = t4.y;
+              uv[4 * q4 + 2] = t4.z;
+              uv[4 * q4 + 3] = t4.w;
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < kPairs; ++m) {
+            const float2 um = make_float2(uv[2 * m], uv[2 * m + 1]);
+            acc[0][m] = ffma2(make_float2(f0[e], f0[e]), um, acc[0][m]);
+            acc[1][m] = ffma2(make_float2(f1[e], f1[e]), um, acc[1][m]);
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < kPairs; ++m) {
+        res[0][2 * m] = acc[0][m].x;
+        res[0][2 * m + 1] = acc[0][m].y;
+        res[1][2 * m] = acc[1][m].x;
+        res[1][2 * m + 1] = acc[1][m].y;
       }
     }
 
+    uint16_t* sc = stage_sc + (it & 1) * G * kTR;
 #pragma unroll
-    for (int rr = 0; rr < kRPT; ++rr) {
-      const int n = n0 + tid + rr * kP1Threads;
-      if (n < p.N) {
-#pragma unroll
-        for (int j = 0; j < G; ++j)
-          p.scores[(static_cast<int64_t>(g) * G + j) * p.s_stride + n] = f32_to_bf16_bits(acc[rr][j]);
+    for (int j = 0; j < G; ++j) {
+      uint32_t b0 = f32_to_bf16_bits(res[0][j]);
+      uint32_t b1 = f32_to_bf16_bits(res[1][j]);
+      if (p.keys_out) {
+        b0 = bf16_order_key(b0);
+        b1 = bf16_order_key(b1);
       }
+      sc[j * kTR + r0] = static_cast<uint16_t>(b0);
+      sc[j * kTR + r1] = static_cast<uint16_t>(b1);
     }
 
-    if (__syncthreads_or(!ok)) break;  // every thread is done reading stage s
-    if (tid == 0 && it + kP1Stages < my_tiles) {
+    if (__syncthreads_or(!ok)) break;  // stage s read; staged scores complete
+    if (tid == 0 && it + kStages < my_tiles) {
       fence_proxy_async_smem();
-      issue(it + kP1Stages);
+      issue(it + kStages);
     }
+    if (it == my_tiles - 1) flush(it);
   }
 }
 
@@ -305,7 +420,7 @@ static int launch_score_t(const void* K, int64_t ksb, int64_t ksh, const P1Param
   constexpr int smem = p1_smem_bytes<T, G>();
   if (ensure_smem_attr(reinterpret_cast<const void*>(&score_kernel<T, G>), smem) != cudaSuccess)
     return DCR_ERR_CUDA;
-  const int max_ctas = device_sm_count() * 2;
+  const int max_ctas = device_sm_count() * Cfg::kCtasPerSm;
   const int grid = p.total_tiles < max_ctas ? p.total_tiles : max_ctas;
   score_kernel<T, G><<<grid, kP1Threads, smem, st>>>(map, p);
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
@@ -325,8 +440,10 @@ static int launch_score_g(const void* K, int64_t ksb, int64_t ksh, const P1Param
 
 int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
                  const float* u, const void* Q, float eps, int B, int H, int H_kv, int N,
-                 uint16_t* scores, int64_t s_stride_row, cudaStream_t st) {
+                 uint16_t* scores, int64_t s_stride_row, int keys_out, cudaStream_t st) {
   P1Params p;
+  p.keys_out = keys_out;
+  p.vec_store = ((reinterpret_cast<uintptr_t>(scores) & 15u) == 0 && (s_stride_row & 7) == 0) ? 1 : 0;
   p.u = u;
   p.q = Q;
   p.eps = eps;
@@ -335,8 +452,7 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
   p.N = N;
   p.H_kv = H_kv;
   const int G = H / H_kv;
-  const int tile_rows = dtype == DCR_DTYPE_F32 ? P1Cfg<float>::kTileRows
-                                               : P1Cfg<__nv_bfloat16>::kTileRows;
+  const int tile_rows = P1Cfg<__nv_bfloat16>::kTileRows;
   p.tiles_per_group = (N + tile_rows - 1) / tile_rows;
   const int64_t total = static_cast<int64_t>(p.tiles_per_group) * B * H_kv;
   if (total > 0x7fffffff) return DCR_ERR_SHAPE;

@@ -13,11 +13,17 @@
 //      the first `need` positions with key == T. The output is the reference's set,
 //      already ascending.
 //
-// One CTA of 1024 threads owns one (b, h) row. The row is read from L2/L1 three times
-// (pass A histogram, pass B low-nibble histogram + per-warp counts, pass D emission).
-// Warp w owns a contiguous segment of the row in passes B and D, so the per-warp counts
-// of pass B give every warp its exclusive output offset, and the warp-level emission in
-// pass D uses ballot/scan prefix sums only.
+// One CTA of 1024 threads owns one (b, h) row. When the row fits (N <= 96K scores, rows
+// 16-byte aligned) one thread brings it into shared memory with a single bulk copy
+// (cp.async.bulk, completion on an mbarrier); otherwise the passes read it from global
+// memory (L2). The row is processed in chunks of 32768 positions:
+//   A. histogram of key >> 4 (4096 bins, shared-memory atomics); a block-wide suffix
+//      scan finds the high bin BH holding the k-th largest key;
+//   B. a 16-bin histogram of key & 15 over the keys in BH gives T and #{key > T};
+//   D. per chunk, thread t owns 32 consecutive positions: it counts its keys > T and
+//      == T, one block-wide exclusive scan of the packed counts gives every thread its
+//      output offset and its rank among the equal keys, and the thread writes its
+//      selected positions in order.
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
 
@@ -26,6 +32,8 @@ namespace dcr {
 constexpr int kP2Threads = 1024;
 constexpr int kP2Warps = kP2Threads / 32;
 constexpr int kHiBins = 4096;
+constexpr int kP2SmemKeys = 96 * 1024;                  // scores staged in shared memory
+constexpr int kP2DynSmem = kP2SmemKeys * 2 + 16;        // + the bulk-copy mbarrier
 
 struct P2Params {
   const uint16_t* scores;
@@ -35,34 +43,26 @@ struct P2Params {
   int32_t* idx;
   int* row_counters;  // Pass 3 split-K tickets reset here (may be null)
   int vec;            // rows are 16-byte aligned: 8 keys per uint4 load
+  int staged;         // the row is bulk-copied into shared memory first
+  int keys_in;        // rows already hold order keys (Pass 1 keys_out), not bf16 bits
 };
 
-// Loads the 8 keys of vector v (positions 8v .. 8v+7); invalid positions (>= N) get
-// valid-bit 0.
-__device__ __forceinline__ void load_keys8(const uint16_t* row, int v, int N, int vec,
-                                           uint32_t (&key)[8], uint32_t& valid) {
-  const int base = v * 8;
-  if (vec && base + 8 <= N) {
-    const uint4 w = *reinterpret_cast<const uint4*>(row + base);
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      key[2 * i] = bf16_order_key(ww[i] & 0xffffu);
-      key[2 * i + 1] = bf16_order_key(ww[i] >> 16);
-    }
-    valid = 0xffu;
-  } else {
-    valid = 0;
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      if (base + e < N) {
-        key[e] = bf16_order_key(row[base + e]);
-        valid |= 1u << e;
-      } else {
-        key[e] = 0;
-      }
-    }
-  }
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Branch-free order key of a raw bf16 score (same map as bf16_order_key): -0 and +0
+// share key 0x8000, every NaN gets 0xffff.
+__device__ __forceinline__ uint32_t order_key_fast(uint32_t x) {
+  x &= 0xffffu;
+  const uint32_t mag = x & 0x7fffu;
+  x = mag ? x : 0u;
+  const uint32_t key = x ^ (((x >> 15) * 0x7fffu) | 0x8000u);
+  return mag > 0x7f80u ? 0xffffu : key;
 }
 
 __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x) {
@@ -75,65 +75,150 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x) {
   return x;
 }
 
+// The row as 16-bit order keys, 8 per 16-byte vector. STAGED: the keys live in shared
+// memory (converted in place by pass A). Otherwise they are read from global memory and
+// converted on every pass; positions >= N read as key 0, which ranks below every real
+// score (the smallest real key, -inf's, is 0x007f), so they are never selected.
+template <bool STAGED>
+struct KeyRow {
+  const uint16_t* g;  // global row (raw bf16 bits, or keys if keys_in)
+  uint16_t* s;        // shared row (keys)
+  int N;
+  int vec;
+  int keys_in;
+  __device__ __forceinline__ uint32_t key_of(uint32_t raw) const {
+    return keys_in ? (raw & 0xffffu) : order_key_fast(raw);
+  }
+  __device__ __forceinline__ void load(int v, uint32_t (&key)[8]) const {
+    if constexpr (STAGED) {
+      const uint4 w = reinterpret_cast<const uint4*>(s)[v];
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        key[2 * i] = ww[i] & 0xffffu;
+        key[2 * i + 1] = ww[i] >> 16;
+      }
+    } else {
+      const int base = v * 8;
+      if (vec && base + 8 <= N) {
+        const uint4 w = *reinterpret_cast<const uint4*>(g + base);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          key[2 * i] = key_of(ww[i]);
+          key[2 * i + 1] = key_of(ww[i] >> 16);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) key[e] = (base + e < N) ? key_of(g[base + e]) : 0u;
+      }
+    }
+  }
+};
+
+template <bool STAGED>
 __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p) {
+  constexpr int kVPT = 4;                                // vectors per thread per chunk
+  constexpr int kChunkVec = kP2Threads * kVPT;           // 4096 vectors = 32768 keys
   __shared__ uint32_t hist[kHiBins];
-  __shared__ uint32_t whist[kP2Warps][16];
-  __shared__ uint32_t wgt_hi[kP2Warps];
+  __shared__ uint32_t hist2[16];
+  __shared__ uint32_t scan_buf[kP2Threads];
   __shared__ uint32_t wsum[kP2Warps];
-  __shared__ uint32_t w_gt_excl[kP2Warps];
-  __shared__ uint32_t w_eq_excl[kP2Warps];
   __shared__ int s_bh, s_above, s_T, s_need;
+  __shared__ uint32_t s_chunk_tot;
+  extern __shared__ __align__(16) uint8_t p2_dyn[];
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int row = blockIdx.x;
-  const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
-  int32_t* out = p.idx + static_cast<int64_t>(row) * p.k;
   const int N = p.N;
   const int k = p.k;
   const int nvec = (N + 7) >> 3;
+  int32_t* out = p.idx + static_cast<int64_t>(row) * p.k;
 
+  KeyRow<STAGED> kr;
+  kr.g = p.scores + static_cast<int64_t>(row) * p.stride;
+  kr.s = reinterpret_cast<uint16_t*>(p2_dyn);
+  kr.N = N;
+  kr.vec = p.vec;
+  kr.keys_in = p.keys_in;
+
+  uint64_t* bar = reinterpret_cast<uint64_t*>(p2_dyn + kP2SmemKeys * 2);
+  if (STAGED && tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    const uint32_t bytes = static_cast<uint32_t>(nvec) * 16u;
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_load(p2_dyn, kr.g, bytes, bar);
+  }
   if (p.row_counters != nullptr && tid == 0) p.row_counters[row] = 0;
   for (int i = tid; i < kHiBins; i += kP2Threads) hist[i] = 0;
-  if (tid < kP2Warps * 16) (&whist[0][0])[tid] = 0;
+  if (tid < 16) hist2[tid] = 0;
   __syncthreads();
 
-  // ---- pass A: histogram of the high 12 bits ------------------------------------------
-  for (int v = tid; v < nvec; v += kP2Threads) {
-    uint32_t key[8], valid;
-    load_keys8(src, v, N, p.vec, key, valid);
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (valid & (1u << e)) atomicAdd(&hist[key[e] >> 4], 1u);
-  }
-  __syncthreads();
-
-  // ---- find the high bin BH: #{hi > BH} < k <= #{hi >= BH} --------------------------
-  // Thread t owns bins 4t..4t+3; an exclusive suffix sum over threads gives #{hi > 4t+3}.
-  {
-    uint32_t h4[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) h4[i] = hist[4 * tid + i];
-    const uint32_t local = h4[0] + h4[1] + h4[2] + h4[3];
-    // Suffix sum = exclusive prefix sum over positions rt = 1023 - tid: thread tid's count
-    // is placed at position rt, the buffer is prefix-scanned in position order, and
-    // thread tid reads its result back from position rt.
-    const int rt = kP2Threads - 1 - tid;
-    __shared__ uint32_t scan_buf[kP2Threads];
-    scan_buf[rt] = local;
-    __syncthreads();
-    const uint32_t x = scan_buf[tid];  // value of the thread with rt == tid
+  // Exclusive prefix sum of x over the CTA (thread order); returns the total in *tot.
+  auto block_excl_scan = [&](uint32_t x, uint32_t* tot) -> uint32_t {
     const uint32_t incl = warp_incl_scan(x);
     if (lane == 31) wsum[warp] = incl;
     __syncthreads();
     if (warp == 0) {
       const uint32_t ws = wsum[lane];
       const uint32_t wi = warp_incl_scan(ws);
-      wsum[lane] = wi - ws;  // exclusive prefix of warp totals
+      wsum[lane] = wi - ws;
+      if (lane == 31) s_chunk_tot = wi;
     }
     __syncthreads();
-    scan_buf[tid] = incl - x + wsum[warp];  // exclusive prefix at position tid (rt order)
+    const uint32_t r = incl - x + wsum[warp];
+    *tot = s_chunk_tot;
+    __syncthreads();  // wsum / s_chunk_tot may be reused by the next scan
+    return r;
+  };
+
+  // ---- pass A: (convert to keys in place and) histogram the high 12 bits ---------------
+  if constexpr (STAGED) {
+    mbar_wait_bounded(bar, 0);
+    uint4* sv = reinterpret_cast<uint4*>(kr.s);
+    for (int v = tid; v < nvec; v += kP2Threads) {
+      uint4 w = sv[v];
+      uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+      const int base = v * 8;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t k0 = p.keys_in ? (ww[i] & 0xffffu) : order_key_fast(ww[i]);
+        uint32_t k1 = p.keys_in ? (ww[i] >> 16) : order_key_fast(ww[i] >> 16);
+        if (base + 2 * i >= N) k0 = 0u;
+        if (base + 2 * i + 1 >= N) k1 = 0u;
+        atomicAdd(&hist[k0 >> 4], 1u);
+        atomicAdd(&hist[k1 >> 4], 1u);
+        ww[i] = k0 | (k1 << 16);
+      }
+      sv[v] = make_uint4(ww[0], ww[1], ww[2], ww[3]);
+    }
+  } else {
+    for (int v = tid; v < nvec; v += kP2Threads) {
+      uint32_t key[8];
+      kr.load(v, key);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(&hist[key[e] >> 4], 1u);
+    }
+  }
+  __syncthreads();
+
+  // ---- find the high bin BH: #{hi > BH} < k <= #{hi >= BH} --------------------------
+  // Thread t owns bins 4t..4t+3. Suffix sum = exclusive prefix sum over positions
+  // rt = 1023 - tid: thread tid's count is placed at position rt, the buffer is
+  // prefix-scanned in position order, and thread tid reads its result back from rt.
+  {
+    uint32_t h4[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h4[i] = hist[4 * tid + i];
+    const int rt = kP2Threads - 1 - tid;
+    scan_buf[rt] = h4[0] + h4[1] + h4[2] + h4[3];
+    __syncthreads();
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan(scan_buf[tid], &tot);
+    scan_buf[tid] = ex;
     __syncthreads();
     uint32_t above = scan_buf[rt];  // #{keys in bins above 4*tid+3}
 #pragma unroll
@@ -149,120 +234,89 @@ __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p)
   __syncthreads();
   const uint32_t bh = static_cast<uint32_t>(s_bh);
 
-  // ---- pass B: per-warp #{hi > BH} and low-nibble histogram of hi == BH --------------
-  const int vpw = (nvec + kP2Warps - 1) / kP2Warps;  // vectors per warp segment
-  const int seg0 = warp * vpw;
-  const int seg1 = min(nvec, seg0 + vpw);
-  {
-    uint32_t gt = 0;
-    for (int v = seg0 + lane; v < seg1; v += 32) {
-      uint32_t key[8], valid;
-      load_keys8(src, v, N, p.vec, key, valid);
+  // ---- pass B: 16-bin histogram of the low nibble of the keys in BH --------------------
+  for (int v = tid; v < nvec; v += kP2Threads) {
+    uint32_t key[8];
+    kr.load(v, key);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (!(valid & (1u << e))) continue;
-        const uint32_t hi = key[e] >> 4;
-        if (hi > bh) ++gt;
-        else if (hi == bh) atomicAdd(&whist[warp][key[e] & 15u], 1u);
-      }
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) gt += __shfl_xor_sync(0xffffffffu, gt, off);
-    if (lane == 0) wgt_hi[warp] = gt;
+    for (int e = 0; e < 8; ++e)
+      if ((key[e] >> 4) == bh) atomicAdd(&hist2[key[e] & 15u], 1u);
   }
   __syncthreads();
-
-  // ---- threshold T, need, per-warp exclusive offsets ---------------------------------
-  if (warp == 0) {
-    // lanes 0..15 total the low-nibble histogram
-    // Lanes 0..15 total the low-nibble histogram of the high bin; every lane then walks
-    // the 16 totals from the top nibble down to the one where the count reaches k.
-    uint32_t tot = 0;
-    if (lane < 16)
-      for (int w = 0; w < kP2Warps; ++w) tot += whist[w][lane];
-    uint32_t t16[16];
-#pragma unroll
-    for (int nib = 0; nib < 16; ++nib) t16[nib] = __shfl_sync(0xffffffffu, tot, nib);
+  if (tid == 0) {
     uint32_t above = static_cast<uint32_t>(s_above);  // #{key >> 4 > BH} < k
-    uint32_t gt_T = above;
     int lo = 0;
-    bool found = false;
-#pragma unroll
     for (int nib = 15; nib >= 0; --nib) {
-      const uint32_t c = t16[nib];
-      if (!found && static_cast<uint32_t>(k) <= above + c) {
+      const uint32_t c = hist2[nib];
+      if (static_cast<uint32_t>(k) <= above + c) {
         lo = nib;
-        gt_T = above;  // #{key > T}
-        found = true;
+        break;
       }
       above += c;
     }
-    const int need = k - static_cast<int>(gt_T);
-    // per-warp counts (lane = warp index)
-    uint32_t wg = wgt_hi[lane];
-    for (int nib = lo + 1; nib < 16; ++nib) wg += whist[lane][nib];
-    const uint32_t we = whist[lane][lo];
-    const uint32_t wg_incl = warp_incl_scan(wg);
-    const uint32_t we_incl = warp_incl_scan(we);
-    w_gt_excl[lane] = wg_incl - wg;
-    w_eq_excl[lane] = we_incl - we;
-    if (lane == 0) {
-      s_T = static_cast<int>((bh << 4) | static_cast<uint32_t>(lo));
-      s_need = need;
-    }
+    s_T = static_cast<int>((bh << 4) | static_cast<uint32_t>(lo));
+    s_need = k - static_cast<int>(above);  // above == #{key > T}
   }
   __syncthreads();
 
-  // ---- pass D: ordered emission -------------------------------------------------------
-  {
-    const uint32_t T = static_cast<uint32_t>(s_T);
-    const int need = s_need;
-    int E = static_cast<int>(w_eq_excl[warp]);  // equal keys before this lane's step
-    int P = static_cast<int>(w_gt_excl[warp]) + min(static_cast<int>(w_eq_excl[warp]), need);
-    for (int vb = seg0; vb < seg1; vb += 32) {
-      const int v = vb + lane;
-      uint32_t gtm = 0, eqm = 0;
-      if (v < seg1) {
-        uint32_t key[8], valid;
-        load_keys8(src, v, N, p.vec, key, valid);
+  // ---- pass D: ordered emission, one 32768-position chunk at a time -------------------
+  const uint32_t T = static_cast<uint32_t>(s_T);
+  const int need = s_need;
+  int E = 0;  // keys == T before the current chunk
+  int P = 0;  // positions emitted before the current chunk
+  for (int c0 = 0; c0 < nvec; c0 += kChunkVec) {
+    const int v0 = c0 + tid * kVPT;
+    uint32_t key[kVPT][8];
+    uint32_t ngt = 0, neq = 0;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          if (!(valid & (1u << e))) continue;
-          if (key[e] > T) gtm |= 1u << e;
-          else if (key[e] == T) eqm |= 1u << e;
+    for (int j = 0; j < kVPT; ++j) {
+      if (v0 + j < nvec) {
+        kr.load(v0 + j, key[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) key[j][e] = 0u;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ngt += key[j][e] > T ? 1u : 0u;
+        neq += key[j][e] == T ? 1u : 0u;
+      }
+    }
+    uint32_t tot;
+    const uint32_t ex = block_excl_scan(ngt | (neq << 16), &tot);
+    const int eq_before = E + static_cast<int>(ex >> 16);
+    // P counts the ties taken before this chunk (min(E, need)); add the ones taken in
+    // this chunk before this thread.
+    int pos = P + static_cast<int>(ex & 0xffffu) + (min(eq_before, need) - min(E, need));
+    int eq_rank = eq_before;
+#pragma unroll
+    for (int j = 0; j < kVPT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t kk = key[j][e];
+        bool sel = kk > T;
+        if (kk == T) {
+          sel = eq_rank < need;
+          ++eq_rank;
+        }
+        if (sel) {
+          if (pos < k) out[pos] = (v0 + j) * 8 + e;
+          else raise_status(DCR_ERR_DEVICE_INDEX);
+          ++pos;
         }
       }
-      const int ne = __popc(eqm);
-      const int eq_incl = static_cast<int>(warp_incl_scan(static_cast<uint32_t>(ne)));
-      const int eq_before = E + eq_incl - ne;
-      int take = need - eq_before;
-      take = take < 0 ? 0 : (take > ne ? ne : take);
-      uint32_t selm = gtm;
-      uint32_t rem = eqm;
-      for (int i = 0; i < take; ++i) {
-        const uint32_t bit = rem & (0u - rem);
-        selm |= bit;
-        rem ^= bit;
-      }
-      const int ns = __popc(selm);
-      const int s_incl = static_cast<int>(warp_incl_scan(static_cast<uint32_t>(ns)));
-      int pos = P + s_incl - ns;
-      while (selm) {
-        const int e = __ffs(selm) - 1;
-        selm &= selm - 1;
-        if (pos < k) out[pos] = v * 8 + e;
-        else raise_status(DCR_ERR_DEVICE_INDEX);
-        ++pos;
-      }
-      E += __shfl_sync(0xffffffffu, eq_incl, 31);
-      P += __shfl_sync(0xffffffffu, s_incl, 31);
     }
+    const int chunk_eq = static_cast<int>(tot >> 16);
+    const int chunk_gt = static_cast<int>(tot & 0xffffu);
+    P += chunk_gt + (min(E + chunk_eq, need) - min(E, need));
+    E += chunk_eq;
   }
 }
 
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
-                  int32_t* idx, int* row_counters, cudaStream_t st) {
+                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st) {
   P2Params p;
+  p.keys_in = keys_in;
   p.scores = scores;
   p.stride = s_stride_row;
   p.N = N;
@@ -270,7 +324,15 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   p.idx = idx;
   p.row_counters = row_counters;
   p.vec = ((reinterpret_cast<uintptr_t>(scores) & 15u) == 0 && (s_stride_row & 7) == 0) ? 1 : 0;
-  select_kernel<<<rows, kP2Threads, 0, st>>>(p);
+  p.staged = (p.vec && N <= kP2SmemKeys) ? 1 : 0;
+  if (p.staged) {
+    if (ensure_smem_attr(reinterpret_cast<const void*>(&select_kernel<true>), kP2DynSmem) !=
+        cudaSuccess)
+      return DCR_ERR_CUDA;
+    select_kernel<true><<<rows, kP2Threads, kP2DynSmem, st>>>(p);
+  } else {
+    select_kernel<false><<<rows, kP2Threads, 0, st>>>(p);
+  }
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }
 

@@ -46,6 +46,9 @@ SIGNATURES = {
                                   _i32, _f32, _vp, _vp, _sz, _vp]),
     "dcr_decode": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32,
                           _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "dcr_decode_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
+                                _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp,
+                                ctypes.POINTER(_vp)]),
     "dcr_read_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
 }
 

@@ -124,6 +124,16 @@ int dcr_decode(const void* Q, const void* K, const void* V, int dtype,
                int B, int H, int H_kv, int N, int D, int k_eff, float eps,
                void* O, void* workspace, size_t workspace_bytes, void* stream);
 
+/* dcr_decode with four caller-created CUDA events (cudaEvent_t cast to void*) recorded on
+ * the stream before Pass 1, between the passes and after Pass 3, for per-pass timing of
+ * exactly the kernels dcr_decode launches. Diagnostic: the reference has no counterpart. */
+int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype,
+                     int64_t k_stride_b, int64_t k_stride_h,
+                     int64_t v_stride_b, int64_t v_stride_h,
+                     int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                     void* O, void* workspace, size_t workspace_bytes, void* stream,
+                     void* const* events);
+
 /* Synchronises the current device and returns (in *status_out) the OR of the device
  * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.
  * Diagnostic: the reference has no counterpart (its kernels have no device status). */
