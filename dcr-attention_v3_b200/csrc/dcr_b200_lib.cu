@@ -5,3 +5,4 @@
 #include "dcr_select.cu"
 #include "dcr_attend.cu"
 #include "dcr_capi.cu"
+#include "dcr_noalloc.cu"

@@ -132,6 +132,8 @@ const char* dcr_status_string(int status) {
     case DCR_ERR_WORKSPACE: return "workspace is NULL or smaller than dcr_workspace_bytes()";
     case DCR_ERR_CUDA: return "a CUDA runtime call failed";
     case DCR_ERR_DEVICE_TIMEOUT: return "device: a bounded wait expired";
+    case DCR_ERR_NOALLOC_LIMIT:
+      return "shape needs more scratch than dcr_decode_noalloc's 16 MiB array; use dcr_decode";
     case DCR_ERR_DEVICE_INDEX: return "device: an index outside [0, N) was skipped";
     default: return "unknown status";
   }

@@ -25,6 +25,7 @@ DCR_ERR_ALIGN = 5
 DCR_ERR_WORKSPACE = 6
 DCR_ERR_CUDA = 7
 DCR_ERR_DEVICE_TIMEOUT = 8
+DCR_ERR_NOALLOC_LIMIT = 9
 DCR_ERR_DEVICE_INDEX = 16
 
 # Every exported symbol with its (restype, argtypes); tests check this list against the
@@ -46,6 +47,8 @@ SIGNATURES = {
                                   _i32, _f32, _vp, _vp, _sz, _vp]),
     "dcr_decode": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32,
                           _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "dcr_decode_noalloc": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32,
+                                  _i32, _i32, _i32, _i32, _f32, _vp, _vp]),
     "dcr_decode_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                                 _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp,
                                 ctypes.POINTER(_vp)]),

@@ -39,6 +39,8 @@ extern "C" {
 
 #define DCR_HEAD_DIM 64
 #define DCR_ABI_VERSION 1
+/* Size of the library-owned scratch array used by dcr_decode_noalloc (16 MiB). */
+#define DCR_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
 typedef enum dcr_dtype {
   DCR_DTYPE_BF16 = 0,
@@ -56,6 +58,7 @@ typedef enum dcr_status {
   DCR_ERR_WORKSPACE = 6,        /* workspace pointer NULL or smaller than required    */
   DCR_ERR_CUDA = 7,             /* a CUDA runtime call failed                         */
   DCR_ERR_DEVICE_TIMEOUT = 8,   /* device status: a bounded wait expired              */
+  DCR_ERR_NOALLOC_LIMIT = 9,    /* shape needs more than DCR_NOALLOC_SCRATCH_BYTES    */
   DCR_ERR_DEVICE_INDEX = 16     /* device status: an index outside [0, N) was skipped */
 } dcr_status;
 
@@ -123,6 +126,22 @@ int dcr_decode(const void* Q, const void* K, const void* V, int dtype,
                int64_t v_stride_b, int64_t v_stride_h,
                int B, int H, int H_kv, int N, int D, int k_eff, float eps,
                void* O, void* workspace, size_t workspace_bytes, void* stream);
+
+/* dcr_decode without a caller workspace, for callers that cannot allocate device memory
+ * where they run a decode step (an engine plugin whose enqueue must not allocate, a host
+ * callback, a serving loop that cannot take cudaMalloc's implicit synchronisation).
+ * No counterpart in the reference: its Python path allocates through torch on every call.
+ * Scratch is a 16 MiB (DCR_NOALLOC_SCRATCH_BYTES) __device__ array inside the library,
+ * held by every GPU that loads the library until exit; shapes whose dcr_workspace_bytes
+ * exceed it return DCR_ERR_NOALLOC_LIMIT and launch nothing. All calls on a device share
+ * the array: calls that overlap on the GPU race, calls ordered on one stream do not.
+ * The first call on a device looks up the array's address; make it before any stream
+ * capture begins. Allocates nothing. */
+int dcr_decode_noalloc(const void* Q, const void* K, const void* V, int dtype,
+                       int64_t k_stride_b, int64_t k_stride_h,
+                       int64_t v_stride_b, int64_t v_stride_h,
+                       int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                       void* O, void* stream);
 
 /* dcr_decode with four caller-created CUDA events (cudaEvent_t cast to void*) recorded on
  * the stream before Pass 1, between the passes and after Pass 3, for per-pass timing of
