@@ -9,7 +9,8 @@ writes 4915). Each step uses a fresh Q and one of 4 distinct layer caches in rot
 seeded inputs with the reference's sink / outlier-channel distribution.
 
 Metric: microseconds per layer-step (lower is better). ``value`` is device time of the
-timed K steps (max over ranks) divided by the steps of all ranks. With N GPUs every rank
+timed K steps, replayed as one CUDA graph (max over ranks), divided by the steps of all
+ranks; the same K steps launched one by one are reported as ``eager_us_per_step``. With N GPUs every rank
 runs its own shard of (b, h_kv) units of the same size (weak scaling, no collective on the
 data path). Also reported: per-kernel times from CUDA events inside a second, instrumented
 timed loop; the roofline of the dominant kernel against the measured HBM bandwidth; the
@@ -239,11 +240,11 @@ def run_gpu_arm(args):
     sp = stream.cuda_stream
     ksb, ksh = H_kv * N * D, N * D
 
-    def step(i):
+    def step(i, stream_ptr=None):
         K, V = caches[i % LAYERS]
         st = lib.dcr_decode(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), V.data_ptr(), dcode,
                             ksb, ksh, ksb, ksh, B, H, H_kv, N, D, k, 1e-12, O.data_ptr(),
-                            ws.data_ptr(), ws_n, sp)
+                            ws.data_ptr(), ws_n, sp if stream_ptr is None else stream_ptr)
         if st:
             raise _lib.DCRError(st, "dcr_decode")
 
@@ -285,7 +286,7 @@ def run_gpu_arm(args):
             if i % 64 == 0:
                 torch.cuda.synchronize(dev)
         barrier()
-        # ---- timed region: exactly `steps` decode steps --------------------------------
+        # ---- timed region (eager launches): exactly `steps` decode steps ---------------
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         barrier()
@@ -294,7 +295,23 @@ def run_gpu_arm(args):
             step(i)
         e1.record(stream)
         barrier()
+        ms_eager = e0.elapsed_time(e1)
+        # ---- timed region (headline): the same `steps` decode steps as one CUDA graph ---
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(steps):
+                step(i, cap.cuda_stream)
+        with torch.cuda.stream(cap):  # replay() launches on the current stream
+            graph.replay()  # untimed warm replay
+            barrier()
+            e0.record(cap)
+            graph.replay()
+            e1.record(cap)
+        barrier()
         ms = e0.elapsed_time(e1)
+        del graph
     clocks = clk.summary()
 
     # ---- instrumented loop: per-kernel CUDA events (same stream) -----------------------
@@ -365,10 +382,10 @@ def run_gpu_arm(args):
     e2e_ms = f0.elapsed_time(f1)
 
     # max over ranks
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, e2e_ms, ms_eager], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = float(t[0]), float(t[1])
+    ms, e2e_ms, ms_eager = float(t[0]), float(t[1]), float(t[2])
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -393,6 +410,8 @@ def run_gpu_arm(args):
                    else "single GPU",
                    "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
                          f"{2 * B * H_kv * N * D * eb / 1e6:.0f} MB",
+                   "launch": "the K timed steps replayed as one CUDA graph",
+                   "eager_us_per_step": round(ms_eager * 1e3 / steps, 3),
                    "clock_soak_s": args.soak},
         "roofline": {"kernel": dom_name, "bound": "hbm", "achieved": dom["gbs"], "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s",

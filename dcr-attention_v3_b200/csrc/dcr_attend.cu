@@ -16,13 +16,15 @@
 // 128-byte row, fully coalesced) into a 3-stage ring of 128-byte-swizzled shared-memory
 // tiles (4 CTAs per SM); the indices of a tile are loaded two iterations before its
 // copies are issued.
-// Warp w owns rows 16w..16w+15 of every tile and keeps its own online-softmax state:
+// Warp w owns rows 16w..16w+15 of every tile and keeps its own online-softmax state
+// (in base 2, with the 1/sqrt(D) scale and log2(e) folded into the scores; the running
+// maximum is only refreshed when a warp vote sees a score more than 2^8 above it):
 // scores use two lanes per row (32 dims each, Q held in registers) and the P.V product
 // one lane per dimension pair, so a tile needs no block barrier besides the stage
 // hand-over. The 4 warp states are merged at the end. Each CTA writes its partial
 // (m, l, o[64]) to the workspace; the last CTA of a (b, h) to finish (atomic ticket,
 // no waiting) merges the S partials:
-//     M = max_s m_s,  O = sum_s e^{m_s - M} o_s / sum_s e^{m_s - M} l_s.
+//     M = max_s m_s,  O = sum_s 2^{m_s - M} o_s / sum_s 2^{m_s - M} l_s.
 // Every gathered index is checked against [0, N); a bad one is skipped (zero row, zero
 // weight) and raises DCR_ERR_DEVICE_INDEX.
 #include <math.h>
@@ -34,6 +36,9 @@ namespace dcr {
 
 constexpr int kP3Threads = 128;
 constexpr int kP3Tile = 64;
+#ifndef DCR_P3_CTAS_PER_SM
+#define DCR_P3_CTAS_PER_SM 4
+#endif
 
 template <typename T>
 struct P3Cfg {
@@ -42,7 +47,7 @@ struct P3Cfg {
   static constexpr int kTileBytes = kP3Tile * kRowBytes;  // one of K or V
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kStages = 3;
-  static constexpr int kMinBlocks = sizeof(T) == 4 ? 2 : 4;  // CTAs per SM
+  static constexpr int kMinBlocks = sizeof(T) == 4 ? 2 : DCR_P3_CTAS_PER_SM;  // CTAs per SM
   static constexpr int kSmem = 1024 + kStages * kStageBytes;
 };
 
@@ -165,7 +170,8 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   // Per-warp online-softmax state: warp w owns rows 16w .. 16w+15 of every tile.
   float m_w = -INFINITY;
   float l_part = 0.0f;       // lanes with half == 0 accumulate their row's weights
-  float o0 = 0.0f, o1 = 0.0f;  // dims 2*lane, 2*lane+1
+  float o0 = 0.0f, o1 = 0.0f;    // dims 2*lane, 2*lane+1 (even rows)
+  float o0b = 0.0f, o1b = 0.0f;  // (odd rows)
   const int r_own = warp * 16 + (lane >> 1);
 
   for (int tt = 0; tt < ntiles; ++tt) {
@@ -193,44 +199,57 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
         acc1 = fmaf(f[e + 1], qf[c * kPer + e + 1], acc1);
       }
     }
+    // z in log2 units: dot * (1/sqrt(64)) * log2(e); p = 2^(z - m) with m the warp's
+    // reference point (its running maximum, kept unless a score exceeds it by 2^8).
     float z = acc0 + acc1;
     z += __shfl_xor_sync(0xffffffffu, z, 1);
-    z *= 0.125f;  // 1 / sqrt(64), exact
+    z *= 0.125f * 1.4426950408889634f;
     const bool valid = tt * kP3Tile + r_own < cnt;
-    float mt = valid ? z : -INFINITY;
+    float alpha = 1.0f;
+    if (__any_sync(0xffffffffu, valid && !(z <= m_w + 8.0f))) {
+      float mt = valid ? z : -INFINITY;
 #pragma unroll
-    for (int off = 2; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
-    const float m_new = fmaxf(m_w, mt);
-    const float alpha = (m_new == -INFINITY) ? 1.0f : expf(m_w - m_new);
-    const float pr = valid ? expf(z - m_new) : 0.0f;
+      for (int off = 2; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float m_new = fmaxf(m_w, mt);
+      alpha = (m_w == -INFINITY) ? 0.0f : exp2f(m_w - m_new);
+      m_w = m_new;
+    }
+    const float pr = valid ? exp2f(z - m_w) : 0.0f;
     if (half == 0) P_s[r_own] = pr;
     l_part = l_part * alpha + (half == 0 ? pr : 0.0f);
-    m_w = m_new;
     __syncwarp();
 
-    // ---- P.V over the warp's rows: lane owns dims 2*lane, 2*lane+1 ----
+    // ---- P.V over the warp's rows: lane owns dims 2*lane, 2*lane+1; even and odd rows
+    // accumulate separately (shorter dependent chains) and are added after the loop ----
     o0 *= alpha;
     o1 *= alpha;
+    o0b *= alpha;
+    o1b *= alpha;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int rr = warp * 16 + i;
       const float pw = P_s[rr];
+      float2 v2;
       if constexpr (sizeof(T) == 4) {
         const uint32_t addr = vt_addr + swz_offset(rr, lane >> 1, kP3Tile) + (lane & 1) * 8;
-        float2 v2;
         asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];" : "=f"(v2.x), "=f"(v2.y) : "r"(addr));
-        o0 = fmaf(pw, v2.x, o0);
-        o1 = fmaf(pw, v2.y, o1);
       } else {
         const uint32_t addr = vt_addr + swz_offset(rr, lane >> 2, kP3Tile) + (lane & 3) * 4;
         uint32_t w;
         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(addr));
-        const float2 v2 = ElemTraits<T>::widen2(w);
+        v2 = ElemTraits<T>::widen2(w);
+      }
+      if (i & 1) {
+        o0b = fmaf(pw, v2.x, o0b);
+        o1b = fmaf(pw, v2.y, o1b);
+      } else {
         o0 = fmaf(pw, v2.x, o0);
         o1 = fmaf(pw, v2.y, o1);
       }
     }
   }
+  o0 += o0b;
+  o1 += o1b;
   cp_async_wait<0>();
 
   // ---- merge the 4 warps' (m, l, o) ----
@@ -251,7 +270,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   float l_cta = 0.0f;
 #pragma unroll
   for (int w = 0; w < kWarps; ++w) {
-    sc[w] = (m_red[w] == -INFINITY) ? 0.0f : expf(m_red[w] - M);
+    sc[w] = (m_red[w] == -INFINITY) ? 0.0f : exp2f(m_red[w] - M);
     l_cta = fmaf(sc[w], l_red[w], l_cta);
   }
   float od = 0.0f;
@@ -285,7 +304,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
     for (int t = 0; t < p.S; ++t) {
       const float* pt = base + t * (kD + 2);
       const float mt = __ldcg(pt);
-      const float w = (mt == -INFINITY) ? 0.0f : expf(mt - Mg);
+      const float w = (mt == -INFINITY) ? 0.0f : exp2f(mt - Mg);
       L = fmaf(w, __ldcg(pt + 1), L);
       o = fmaf(w, __ldcg(pt + 2 + tid), o);
     }
@@ -295,7 +314,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
 }
 
 int attend_splits(int rows, int k_eff) {
-  const int slots = device_sm_count() * 4;  // 4 CTAs per SM (16-bit caches)
+  const int slots = device_sm_count() * DCR_P3_CTAS_PER_SM;  // resident CTAs (16-bit caches)
   int S = slots / (rows > 0 ? rows : 1);
   const int max_by_tiles = (k_eff + kP3Tile - 1) / kP3Tile;
   if (S > max_by_tiles) S = max_by_tiles;

@@ -17,6 +17,25 @@ int device_sm_count();
 // Sets the dynamic shared-memory limit of a kernel once per (kernel, device).
 cudaError_t ensure_smem_attr(const void* func, int bytes);
 
+// Launches a kernel as a grid of 1-D thread-block clusters of `cluster` CTAs.
+template <typename Kernel, typename... Args>
+cudaError_t launch_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                           int cluster, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Split-K factor used by Pass 3 for this shape (1 = no split, no workspace partials).
 int attend_splits(int rows, int k_eff);
 

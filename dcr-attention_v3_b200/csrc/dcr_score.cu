@@ -99,28 +99,45 @@ int launch_unit_query(const void* Q, int dtype, int rows, float eps, float* u, c
 // ---------------------------------------------------------------------------------------
 // Pass 1
 // ---------------------------------------------------------------------------------------
-constexpr int kP1Threads = 128;
+// Launch shape of Pass 1 (compile-time; overridable for tuning sweeps).
+#ifndef DCR_P1_THREADS
+#define DCR_P1_THREADS 128
+#endif
+#ifndef DCR_P1_RPT
+#define DCR_P1_RPT 2
+#endif
+#ifndef DCR_P1_STAGES
+#define DCR_P1_STAGES 2
+#endif
+constexpr int kP1Threads = DCR_P1_THREADS;
 
 template <typename T>
 struct P1Cfg {
-  static constexpr int kRPT = 2;                        // rows per thread per tile
-  static constexpr int kTileRows = kP1Threads * kRPT;   // 256
-  static constexpr int kStageBytes = kTileRows * RowTraits<T>::kRowBytes;  // 32 / 64 KiB
-  static constexpr int kStages = sizeof(T) == 4 ? 2 : 3;
-  static constexpr int kCtasPerSm = sizeof(T) == 4 ? 1 : 2;
+  static constexpr int kRPT = DCR_P1_RPT;               // rows per thread per tile
+  static constexpr int kTileRows = kP1Threads * kRPT;   // <= 256 (TMA box limit)
+  static constexpr int kStageBytes = kTileRows * RowTraits<T>::kRowBytes;
+  static constexpr int kStages = sizeof(T) == 4 ? 2 : DCR_P1_STAGES;
   static constexpr int kBoxCols = 128 / ElemTraits<T>::kBytes;            // 64 or 32
+  static_assert(kTileRows <= 256, "TMA box height is at most 256 rows");
 };
 
-template <int G>
-__host__ __device__ constexpr int p1_u_bytes() {
-  return G == 1 ? kD * 8 : G * kD * 4;  // {u, u} pairs, or u_t[d][G]
-}
+__host__ __device__ constexpr int p1_u_bytes(int G) { return G * kD * 4; }  // u_t[d][G]
 
 template <typename T, int G>
 __host__ __device__ constexpr int p1_smem_bytes() {
-  // tiles + unit queries + double-buffered score staging [2][G][256] u16 + mbarriers
-  return 1024 + P1Cfg<T>::kStages * P1Cfg<T>::kStageBytes + p1_u_bytes<G>() +
+  // tiles + unit queries + double-buffered score staging [2][G][tile] u16 + mbarriers
+  return 1024 + P1Cfg<T>::kStages * P1Cfg<T>::kStageBytes + p1_u_bytes(G) +
          2 * G * P1Cfg<T>::kTileRows * 2 + P1Cfg<T>::kStages * 8;
+}
+
+// Resident CTAs per SM allowed by shared memory (228 KB per SM, 1 KB reserved per CTA).
+template <typename T, int G>
+__host__ __device__ constexpr int p1_ctas_per_sm() {
+  return (233472 / (p1_smem_bytes<T, G>() + 1024)) < 1
+             ? 1
+             : ((233472 / (p1_smem_bytes<T, G>() + 1024)) > 4
+                    ? 4
+                    : (233472 / (p1_smem_bytes<T, G>() + 1024)));
 }
 
 // Two IEEE fused multiply-adds in one instruction: {a.x*b.x + c.x, a.y*b.y + c.y}.
@@ -161,20 +178,21 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, ui
 }
 
 template <typename T, int G>
-__global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
+__global__ void __launch_bounds__(kP1Threads, (p1_ctas_per_sm<T, G>()))
     score_kernel(const __grid_constant__ CUtensorMap kmap, const P1Params p) {
   using Cfg = P1Cfg<T>;
   constexpr int kChunks = RowTraits<T>::kChunks;
   constexpr int kPer = ElemTraits<T>::kPerChunk;
   constexpr int kStages = Cfg::kStages;
   constexpr int kTR = Cfg::kTileRows;
+  constexpr int kRPT = Cfg::kRPT;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* tiles = smem;
-  float* u_s = reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes);
-  uint16_t* stage_sc = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(u_s) + p1_u_bytes<G>());
+  float* u_s = reinterpret_cast<float*>(smem + kStages * Cfg::kStageBytes);  // u_t[d][G]
+  uint16_t* stage_sc = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(u_s) + p1_u_bytes(G));
   uint64_t* full = reinterpret_cast<uint64_t*>(stage_sc + 2 * G * kTR);
 
   const int tid = threadIdx.x;
@@ -209,13 +227,12 @@ __global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
     for (int sub = 0; sub < RowTraits<T>::kSubTiles; ++sub)
       tma_load_4d(dst + sub * kTR * 128, &kmap, &full[s], sub * Cfg::kBoxCols, n0, hk, b);
   };
-  // Writes the staged scores of tile `it` (buffer it & 1) to global memory: thread t
-  // stores 8 consecutive scores of one head row per pass.
+  // Writes the staged scores of tile `it` (buffer it & 1) to global memory: each pass of
+  // the loop stores 8 consecutive scores of one head row per thread.
   auto flush = [&](int it) {
     int g, n0;
     tile_of(it, g, n0);
     const uint16_t* src = stage_sc + (it & 1) * G * kTR;
-#pragma unroll
     for (int i = tid; i < G * kTR / 8; i += kP1Threads) {
       const int j = i / (kTR / 8);
       const int r = (i - j * (kTR / 8)) * 8;
@@ -250,24 +267,11 @@ __global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
       for (int j = warp; j < G; j += kP1Threads / 32) {
         if (p.u != nullptr) {
           const float* src = p.u + (static_cast<size_t>(g) * G + j) * kD;
-          for (int d = tid & 31; d < kD; d += 32) {
-            if (G == 1) {
-              u_s[2 * d] = src[d];
-              u_s[2 * d + 1] = src[d];
-            } else {
-              u_s[d * G + j] = src[d];
-            }
-          }
+          for (int d = tid & 31; d < kD; d += 32) u_s[d * G + j] = src[d];
         } else {
           const char* q_row = static_cast<const char*>(p.q) +
                               (static_cast<size_t>(g) * G + j) * kD * sizeof(T);
-          if (G == 1) {
-            unit_query_warp<T>(q_row, p.eps, u_s, 2);
-            __syncwarp();
-            for (int d = tid & 31; d < kD; d += 32) u_s[2 * d + 1] = u_s[2 * d];
-          } else {
-            unit_query_warp<T>(q_row, p.eps, u_s + j, G);
-          }
+          unit_query_warp<T>(q_row, p.eps, u_s + j, G);
         }
       }
       __syncthreads();
@@ -277,43 +281,50 @@ __global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
     if (it > 0) flush(it - 1);  // scores of the previous tile, staged before the barrier
 
     const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it / kStages) & 1));
-
     const uint32_t tile_addr = smem_u32(tiles + s * Cfg::kStageBytes);
-    const int r0 = tid;
-    const int r1 = tid + kP1Threads;
-    float res[2][G];  // [row][head]
+    float res[kRPT][G];  // [row][head]
 
     if constexpr (G == 1) {
-      // pair = (row r0, row r1) of the single head; u_s holds {u, u}
-      float2 acc = make_float2(0.0f, 0.0f);
+      // one query head: a plain fmaf chain per row
+      float acc[kRPT];
+#pragma unroll
+      for (int i = 0; i < kRPT; ++i) acc[i] = 0.0f;
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
-        float f0[kPer], f1[kPer];
-        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r0, c, kTR)), f0);
-        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r1, c, kTR)), f1);
-        const float4* ud = reinterpret_cast<const float4*>(u_s + c * kPer * 2);
+        const float4* ud = reinterpret_cast<const float4*>(u_s + c * kPer);
+        float uv[kPer];
 #pragma unroll
-        for (int q = 0; q < kPer / 2; ++q) {
-          const float4 t4 = ud[q];
-          acc = ffma2(make_float2(f0[2 * q], f1[2 * q]), make_float2(t4.x, t4.y), acc);
-          acc = ffma2(make_float2(f0[2 * q + 1], f1[2 * q + 1]), make_float2(t4.z, t4.w), acc);
+        for (int q4 = 0; q4 < kPer / 4; ++q4) {
+          const float4 t4 = ud[q4];
+          uv[4 * q4] = t4.x;
+          uv[4 * q4 + 1] = t4.y;
+          uv[4 * q4 + 2] = t4.z;
+          uv[4 * q4 + 3] = t4.w;
+        }
+#pragma unroll
+        for (int i = 0; i < kRPT; ++i) {
+          float f[kPer];
+          ElemTraits<T>::widen(lds128(tile_addr + swz_offset(tid + i * kP1Threads, c, kTR)), f);
+#pragma unroll
+          for (int e = 0; e < kPer; ++e) acc[i] = fmaf(f[e], uv[e], acc[i]);
         }
       }
-      res[0][0] = acc.x;
-      res[1][0] = acc.y;
+#pragma unroll
+      for (int i = 0; i < kRPT; ++i) res[i][0] = acc[i];
     } else {
-      // pair = (head 2m, head 2m+1) of one row; u_s is u_t[d][G]
+      // pair = (head 2m, head 2m+1) of one row, advanced by one packed FMA
       constexpr int kPairs = G / 2;
-      float2 acc[2][kPairs];
+      float2 acc[kRPT][kPairs];
 #pragma unroll
-      for (int rr = 0; rr < 2; ++rr)
+      for (int i = 0; i < kRPT; ++i)
 #pragma unroll
-        for (int m = 0; m < kPairs; ++m) acc[rr][m] = make_float2(0.0f, 0.0f);
+        for (int m = 0; m < kPairs; ++m) acc[i][m] = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int c = 0; c < kChunks; ++c) {
-        float f0[kPer], f1[kPer];
-        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r0, c, kTR)), f0);
-        ElemTraits<T>::widen(lds128(tile_addr + swz_offset(r1, c, kTR)), f1);
+        float f[kRPT][kPer];
+#pragma unroll
+        for (int i = 0; i < kRPT; ++i)
+          ElemTraits<T>::widen(lds128(tile_addr + swz_offset(tid + i * kP1Threads, c, kTR)), f[i]);
 #pragma unroll
         for (int e = 0; e < kPer; ++e) {
           const float* ud = u_s + (c * kPer + e) * G;
@@ -335,32 +346,30 @@ __global__ void __launch_bounds__(kP1Threads, P1Cfg<T>::kCtasPerSm)
 #pragma unroll
           for (int m = 0; m < kPairs; ++m) {
             const float2 um = make_float2(uv[2 * m], uv[2 * m + 1]);
-            acc[0][m] = ffma2(make_float2(f0[e], f0[e]), um, acc[0][m]);
-            acc[1][m] = ffma2(make_float2(f1[e], f1[e]), um, acc[1][m]);
+#pragma unroll
+            for (int i = 0; i < kRPT; ++i)
+              acc[i][m] = ffma2(make_float2(f[i][e], f[i][e]), um, acc[i][m]);
           }
         }
       }
 #pragma unroll
-      for (int m = 0; m < kPairs; ++m) {
-        res[0][2 * m] = acc[0][m].x;
-        res[0][2 * m + 1] = acc[0][m].y;
-        res[1][2 * m] = acc[1][m].x;
-        res[1][2 * m + 1] = acc[1][m].y;
-      }
+      for (int i = 0; i < kRPT; ++i)
+#pragma unroll
+        for (int m = 0; m < kPairs; ++m) {
+          res[i][2 * m] = acc[i][m].x;
+          res[i][2 * m + 1] = acc[i][m].y;
+        }
     }
 
     uint16_t* sc = stage_sc + (it & 1) * G * kTR;
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      uint32_t b0 = f32_to_bf16_bits(res[0][j]);
-      uint32_t b1 = f32_to_bf16_bits(res[1][j]);
-      if (p.keys_out) {
-        b0 = bf16_order_key(b0);
-        b1 = bf16_order_key(b1);
+    for (int i = 0; i < kRPT; ++i)
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        uint32_t bits = f32_to_bf16_bits(res[i][j]);
+        if (p.keys_out) bits = bf16_order_key(bits);
+        sc[j * kTR + tid + i * kP1Threads] = static_cast<uint16_t>(bits);
       }
-      sc[j * kTR + r0] = static_cast<uint16_t>(b0);
-      sc[j * kTR + r1] = static_cast<uint16_t>(b1);
-    }
 
     if (__syncthreads_or(!ok)) break;  // stage s read; staged scores complete
     if (tid == 0 && it + kStages < my_tiles) {
@@ -420,7 +429,7 @@ static int launch_score_t(const void* K, int64_t ksb, int64_t ksh, const P1Param
   constexpr int smem = p1_smem_bytes<T, G>();
   if (ensure_smem_attr(reinterpret_cast<const void*>(&score_kernel<T, G>), smem) != cudaSuccess)
     return DCR_ERR_CUDA;
-  const int max_ctas = device_sm_count() * Cfg::kCtasPerSm;
+  const int max_ctas = device_sm_count() * p1_ctas_per_sm<T, G>();
   const int grid = p.total_tiles < max_ctas ? p.total_tiles : max_ctas;
   score_kernel<T, G><<<grid, kP1Threads, smem, st>>>(map, p);
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
@@ -452,7 +461,7 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
   p.N = N;
   p.H_kv = H_kv;
   const int G = H / H_kv;
-  const int tile_rows = P1Cfg<__nv_bfloat16>::kTileRows;
+  const int tile_rows = P1Cfg<__nv_bfloat16>::kTileRows;  // same for every dtype
   p.tiles_per_group = (N + tile_rows - 1) / tile_rows;
   const int64_t total = static_cast<int64_t>(p.tiles_per_group) * B * H_kv;
   if (total > 0x7fffffff) return DCR_ERR_SHAPE;

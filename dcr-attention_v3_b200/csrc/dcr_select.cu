@@ -7,33 +7,34 @@
 // needed to produce that set in ascending order:
 //
 //   1. Map each bf16 score to an order-preserving 16-bit key (-0 -> +0, NaN -> top).
-//   2. Radix-select the k-th largest key T: a 4096-bin histogram of key >> 4, then a
-//      16-bin histogram of key & 15 inside the chosen high bin.
+//   2. Radix-select the k-th largest key T in two 8-bit levels: a 256-bin histogram of
+//      key >> 8 gives the high byte BH of T, then a 256-bin histogram of the low byte of
+//      the keys in BH gives T.
 //   3. need = k_eff - #{key > T}. Emit, in index order, every position with key > T and
 //      the first `need` positions with key == T. The output is the reference's set,
 //      already ascending.
 //
-// One CTA of 1024 threads owns one (b, h) row. When the row fits (N <= 96K scores, rows
-// 16-byte aligned) one thread brings it into shared memory with a single bulk copy
-// (cp.async.bulk, completion on an mbarrier); otherwise the passes read it from global
-// memory (L2). The row is processed in chunks of 32768 positions:
-//   A. histogram of key >> 4 (4096 bins, shared-memory atomics); a block-wide suffix
-//      scan finds the high bin BH holding the k-th largest key;
-//   B. a 16-bin histogram of key & 15 over the keys in BH gives T and #{key > T};
-//   D. per chunk, thread t owns 32 consecutive positions: it counts its keys > T and
-//      == T, one block-wide exclusive scan of the packed counts gives every thread its
-//      output offset and its rank among the equal keys, and the thread writes its
-//      selected positions in order.
+// Design (B200): a row is processed by one CTA of 512 threads, or, for long rows or few
+// rows, by a thread-block cluster of C CTAs (C = 1..8) that splits it into contiguous
+// segments. Each thread keeps a contiguous run of up to 64 keys in registers (loaded
+// once from L2, where Pass 1 just wrote them). Histograms are built with shared-memory
+// atomics and, in a cluster, added into CTA 0 through distributed shared memory; CTA 0's
+// bins are scanned by one warp. The per-CTA counts of keys > T and == T are exchanged
+// through CTA 0, and a block-wide exclusive scan of the packed per-thread counts gives
+// every thread its output offset and its rank among the equal keys. Threads emit their
+// selected positions from bit masks.
+#include <cooperative_groups.h>
+
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
 
+namespace cg = cooperative_groups;
+
 namespace dcr {
 
-constexpr int kP2Threads = 1024;
+constexpr int kP2Threads = 512;
 constexpr int kP2Warps = kP2Threads / 32;
-constexpr int kHiBins = 4096;
-constexpr int kP2SmemKeys = 96 * 1024;                  // scores staged in shared memory
-constexpr int kP2DynSmem = kP2SmemKeys * 2 + 16;        // + the bulk-copy mbarrier
+constexpr int kP2MaxCluster = 8;
 
 struct P2Params {
   const uint16_t* scores;
@@ -41,19 +42,11 @@ struct P2Params {
   int N;
   int k;
   int32_t* idx;
-  int* row_counters;  // Pass 3 split-K tickets reset here (may be null)
-  int vec;            // rows are 16-byte aligned: 8 keys per uint4 load
-  int staged;         // the row is bulk-copied into shared memory first
-  int keys_in;        // rows already hold order keys (Pass 1 keys_out), not bf16 bits
+  int* row_counters;      // Pass 3 split-K tickets reset here (may be null)
+  int vec;                // rows are 16-byte aligned: 8 keys per uint4 load
+  int keys_in;            // rows already hold order keys (Pass 1 keys_out), not bf16 bits
+  int seg_vec;            // vectors (8 positions) per CTA segment
 };
-
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
-                                          uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Branch-free order key of a raw bf16 score (same map as bf16_order_key): -0 and +0
 // share key 0x8000, every NaN gets 0xffff.
@@ -75,265 +68,269 @@ __device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x) {
   return x;
 }
 
-// The row as 16-bit order keys, 8 per 16-byte vector. STAGED: the keys live in shared
-// memory (converted in place by pass A). Otherwise they are read from global memory and
-// converted on every pass; positions >= N read as key 0, which ranks below every real
-// score (the smallest real key, -inf's, is 0x007f), so they are never selected.
-template <bool STAGED>
-struct KeyRow {
-  const uint16_t* g;  // global row (raw bf16 bits, or keys if keys_in)
-  uint16_t* s;        // shared row (keys)
-  int N;
-  int vec;
-  int keys_in;
-  __device__ __forceinline__ uint32_t key_of(uint32_t raw) const {
-    return keys_in ? (raw & 0xffffu) : order_key_fast(raw);
+// One warp finds, in a 256-bin histogram h, the bin B with #{above B} < k <= #{above B-1}
+// (counting from the top) and returns B and above = #{keys in bins above B}.
+__device__ __forceinline__ void warp_find_bin(const uint32_t* h, uint32_t k, int& bin,
+                                              uint32_t& above) {
+  const int lane = threadIdx.x & 31;
+  uint32_t c[8];
+  uint32_t tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    c[i] = h[8 * lane + i];
+    tot += c[i];
   }
-  __device__ __forceinline__ void load(int v, uint32_t (&key)[8]) const {
-    if constexpr (STAGED) {
-      const uint4 w = reinterpret_cast<const uint4*>(s)[v];
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  // inclusive suffix sum over lanes: sum of tot over lanes >= lane
+  uint32_t suf = tot;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        key[2 * i] = ww[i] & 0xffffu;
-        key[2 * i + 1] = ww[i] >> 16;
-      }
-    } else {
-      const int base = v * 8;
-      if (vec && base + 8 <= N) {
-        const uint4 w = *reinterpret_cast<const uint4*>(g + base);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  for (int off = 1; off < 32; off <<= 1) {
+    const uint32_t y = __shfl_down_sync(0xffffffffu, suf, off);
+    if (lane + off < 32) suf += y;
+  }
+  uint32_t a = suf - tot;  // keys in bins above this lane's 8 bins
+  int found = -1;
+  uint32_t found_above = 0;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          key[2 * i] = key_of(ww[i]);
-          key[2 * i + 1] = key_of(ww[i] >> 16);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) key[e] = (base + e < N) ? key_of(g[base + e]) : 0u;
-      }
+  for (int i = 7; i >= 0; --i) {
+    if (found < 0 && a < k && k <= a + c[i]) {
+      found = 8 * lane + i;
+      found_above = a;
     }
+    a += c[i];
   }
-};
+  const unsigned m = __ballot_sync(0xffffffffu, found >= 0);
+  const int src = m ? (__ffs(m) - 1) : 0;
+  bin = __shfl_sync(0xffffffffu, found, src);
+  above = __shfl_sync(0xffffffffu, found_above, src);
+}
 
-template <bool STAGED>
+// VPT: vectors (8 positions each) per thread, 1..8.
+template <int VPT>
 __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p) {
-  constexpr int kVPT = 4;                                // vectors per thread per chunk
-  constexpr int kChunkVec = kP2Threads * kVPT;           // 4096 vectors = 32768 keys
-  __shared__ uint32_t hist[kHiBins];
-  __shared__ uint32_t hist2[16];
-  __shared__ uint32_t scan_buf[kP2Threads];
+  constexpr int kKeys = VPT * 8;
+  constexpr int kWords = (kKeys + 31) / 32;
+  __shared__ uint32_t hist_hi[256];
+  __shared__ uint32_t hist_lo[256];
   __shared__ uint32_t wsum[kP2Warps];
-  __shared__ int s_bh, s_above, s_T, s_need;
-  __shared__ uint32_t s_chunk_tot;
-  extern __shared__ __align__(16) uint8_t p2_dyn[];
+  __shared__ uint32_t scan_tot;
+  __shared__ uint32_t cta_gt[kP2MaxCluster];
+  __shared__ uint32_t cta_eq[kP2MaxCluster];
+  __shared__ int s_bh;
+  __shared__ uint32_t s_above;
 
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = static_cast<int>(cluster.num_blocks());
+  const int crank = static_cast<int>(cluster.block_rank());
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int row = blockIdx.x;
+  const int row = blockIdx.x / C;
   const int N = p.N;
   const int k = p.k;
   const int nvec = (N + 7) >> 3;
-  int32_t* out = p.idx + static_cast<int64_t>(row) * p.k;
+  const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
 
-  KeyRow<STAGED> kr;
-  kr.g = p.scores + static_cast<int64_t>(row) * p.stride;
-  kr.s = reinterpret_cast<uint16_t*>(p2_dyn);
-  kr.N = N;
-  kr.vec = p.vec;
-  kr.keys_in = p.keys_in;
+  uint32_t* hist_hi0 = cluster.map_shared_rank(hist_hi, 0);
+  uint32_t* hist_lo0 = cluster.map_shared_rank(hist_lo, 0);
+  uint32_t* gt0 = cluster.map_shared_rank(cta_gt, 0);
+  uint32_t* eq0 = cluster.map_shared_rank(cta_eq, 0);
+  int* bh0 = cluster.map_shared_rank(&s_bh, 0);
+  uint32_t* above0 = cluster.map_shared_rank(&s_above, 0);
 
-  uint64_t* bar = reinterpret_cast<uint64_t*>(p2_dyn + kP2SmemKeys * 2);
-  if (STAGED && tid == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-    const uint32_t bytes = static_cast<uint32_t>(nvec) * 16u;
-    mbar_arrive_expect_tx(bar, bytes);
-    bulk_load(p2_dyn, kr.g, bytes, bar);
+  if (crank == 0 && tid == 0 && p.row_counters != nullptr) p.row_counters[row] = 0;
+  if (tid < 256) {
+    hist_lo[tid] = 0;
+    hist_hi[tid] = 0;
   }
-  if (p.row_counters != nullptr && tid == 0) p.row_counters[row] = 0;
-  for (int i = tid; i < kHiBins; i += kP2Threads) hist[i] = 0;
-  if (tid < 16) hist2[tid] = 0;
-  __syncthreads();
 
-  // Exclusive prefix sum of x over the CTA (thread order); returns the total in *tot.
-  auto block_excl_scan = [&](uint32_t x, uint32_t* tot) -> uint32_t {
-    const uint32_t incl = warp_incl_scan(x);
-    if (lane == 31) wsum[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      const uint32_t ws = wsum[lane];
-      const uint32_t wi = warp_incl_scan(ws);
-      wsum[lane] = wi - ws;
-      if (lane == 31) s_chunk_tot = wi;
-    }
-    __syncthreads();
-    const uint32_t r = incl - x + wsum[warp];
-    *tot = s_chunk_tot;
-    __syncthreads();  // wsum / s_chunk_tot may be reused by the next scan
-    return r;
-  };
-
-  // ---- pass A: (convert to keys in place and) histogram the high 12 bits ---------------
-  if constexpr (STAGED) {
-    mbar_wait_bounded(bar, 0);
-    uint4* sv = reinterpret_cast<uint4*>(kr.s);
-    for (int v = tid; v < nvec; v += kP2Threads) {
-      uint4 w = sv[v];
-      uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-      const int base = v * 8;
+  // ---- keys of this thread: positions [v0 * 8, (v0 + VPT) * 8), 0 past the segment ----
+  // Key 0 ranks below every real score (the smallest real key, -inf's, is 0x007f), so
+  // padding is never selected.
+  const int v_begin = crank * p.seg_vec;
+  const int v_end = min(nvec, v_begin + p.seg_vec);
+  const int v0 = v_begin + tid * VPT;
+  uint32_t key[kKeys];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = v0 + j;
+    const int base = v * 8;
+    if (v < v_end && p.vec && base + 8 <= N) {
+      const uint4 w = *reinterpret_cast<const uint4*>(src + base);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        uint32_t k0 = p.keys_in ? (ww[i] & 0xffffu) : order_key_fast(ww[i]);
-        uint32_t k1 = p.keys_in ? (ww[i] >> 16) : order_key_fast(ww[i] >> 16);
-        if (base + 2 * i >= N) k0 = 0u;
-        if (base + 2 * i + 1 >= N) k1 = 0u;
-        atomicAdd(&hist[k0 >> 4], 1u);
-        atomicAdd(&hist[k1 >> 4], 1u);
-        ww[i] = k0 | (k1 << 16);
+        key[8 * j + 2 * i] = p.keys_in ? (ww[i] & 0xffffu) : order_key_fast(ww[i]);
+        key[8 * j + 2 * i + 1] = p.keys_in ? (ww[i] >> 16) : order_key_fast(ww[i] >> 16);
       }
-      sv[v] = make_uint4(ww[0], ww[1], ww[2], ww[3]);
-    }
-  } else {
-    for (int v = tid; v < nvec; v += kP2Threads) {
-      uint32_t key[8];
-      kr.load(v, key);
+    } else {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) atomicAdd(&hist[key[e] >> 4], 1u);
+      for (int e = 0; e < 8; ++e) {
+        uint32_t kk = 0u;
+        if (v < v_end && base + e < N) {
+          const uint32_t raw = src[base + e];
+          kk = p.keys_in ? raw : order_key_fast(raw);
+        }
+        key[8 * j + e] = kk;
+      }
     }
   }
-  __syncthreads();
+  cluster.sync();  // histograms initialised everywhere before anyone adds into CTA 0's
 
-  // ---- find the high bin BH: #{hi > BH} < k <= #{hi >= BH} --------------------------
-  // Thread t owns bins 4t..4t+3. Suffix sum = exclusive prefix sum over positions
-  // rt = 1023 - tid: thread tid's count is placed at position rt, the buffer is
-  // prefix-scanned in position order, and thread tid reads its result back from rt.
-  {
-    uint32_t h4[4];
+  // ---- level 1: histogram of the high byte, added into CTA 0 -------------------------
 #pragma unroll
-    for (int i = 0; i < 4; ++i) h4[i] = hist[4 * tid + i];
-    const int rt = kP2Threads - 1 - tid;
-    scan_buf[rt] = h4[0] + h4[1] + h4[2] + h4[3];
+  for (int e = 0; e < kKeys; ++e)
+    if (key[e] != 0u) atomicAdd(&hist_hi[key[e] >> 8], 1u);
+  if (C > 1) {
     __syncthreads();
-    uint32_t tot;
-    const uint32_t ex = block_excl_scan(scan_buf[tid], &tot);
-    scan_buf[tid] = ex;
+    if (crank != 0 && tid < 256 && hist_hi[tid]) atomicAdd(hist_hi0 + tid, hist_hi[tid]);
+  }
+  cluster.sync();
+  if (crank == 0 && warp == 0) {
+    int bin;
+    uint32_t above;
+    warp_find_bin(hist_hi, static_cast<uint32_t>(k), bin, above);
+    if (lane == 0) {
+      s_bh = bin;
+      s_above = above;
+    }
+  }
+  cluster.sync();
+  const uint32_t bh = static_cast<uint32_t>(*bh0);
+
+  // ---- level 2: low byte of the keys in BH --------------------------------------------
+#pragma unroll
+  for (int e = 0; e < kKeys; ++e)
+    if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist_lo[key[e] & 0xffu], 1u);
+  if (C > 1) {
     __syncthreads();
-    uint32_t above = scan_buf[rt];  // #{keys in bins above 4*tid+3}
-#pragma unroll
-    for (int i = 3; i >= 0; --i) {
-      const uint32_t c = h4[i];
-      if (above < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= above + c) {
-        s_bh = 4 * tid + i;
-        s_above = static_cast<int>(above);
-      }
-      above += c;
+    if (crank != 0 && tid < 256 && hist_lo[tid]) atomicAdd(hist_lo0 + tid, hist_lo[tid]);
+  }
+  cluster.sync();
+
+  // T and need: every CTA's warp 0 scans CTA 0's low-byte histogram
+  __shared__ uint32_t s_T;
+  __shared__ int s_need;
+  if (warp == 0) {
+    int lo;
+    uint32_t above_lo;
+    warp_find_bin(hist_lo0, static_cast<uint32_t>(k) - *above0, lo, above_lo);
+    if (lane == 0) {
+      s_T = (bh << 8) | static_cast<uint32_t>(lo);
+      s_need = k - static_cast<int>(*above0 + above_lo);  // minus #{key > T}
     }
   }
   __syncthreads();
-  const uint32_t bh = static_cast<uint32_t>(s_bh);
-
-  // ---- pass B: 16-bin histogram of the low nibble of the keys in BH --------------------
-  for (int v = tid; v < nvec; v += kP2Threads) {
-    uint32_t key[8];
-    kr.load(v, key);
-#pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if ((key[e] >> 4) == bh) atomicAdd(&hist2[key[e] & 15u], 1u);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    uint32_t above = static_cast<uint32_t>(s_above);  // #{key >> 4 > BH} < k
-    int lo = 0;
-    for (int nib = 15; nib >= 0; --nib) {
-      const uint32_t c = hist2[nib];
-      if (static_cast<uint32_t>(k) <= above + c) {
-        lo = nib;
-        break;
-      }
-      above += c;
-    }
-    s_T = static_cast<int>((bh << 4) | static_cast<uint32_t>(lo));
-    s_need = k - static_cast<int>(above);  // above == #{key > T}
-  }
-  __syncthreads();
-
-  // ---- pass D: ordered emission, one 32768-position chunk at a time -------------------
-  const uint32_t T = static_cast<uint32_t>(s_T);
+  const uint32_t T = s_T;
   const int need = s_need;
-  int E = 0;  // keys == T before the current chunk
-  int P = 0;  // positions emitted before the current chunk
-  for (int c0 = 0; c0 < nvec; c0 += kChunkVec) {
-    const int v0 = c0 + tid * kVPT;
-    uint32_t key[kVPT][8];
-    uint32_t ngt = 0, neq = 0;
+
+  // ---- per-thread masks and counts ----------------------------------------------------
+  uint32_t gtm[kWords], eqm[kWords];
 #pragma unroll
-    for (int j = 0; j < kVPT; ++j) {
-      if (v0 + j < nvec) {
-        kr.load(v0 + j, key[j]);
-      } else {
+  for (int w = 0; w < kWords; ++w) gtm[w] = eqm[w] = 0u;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) key[j][e] = 0u;
-      }
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        ngt += key[j][e] > T ? 1u : 0u;
-        neq += key[j][e] == T ? 1u : 0u;
-      }
-    }
-    uint32_t tot;
-    const uint32_t ex = block_excl_scan(ngt | (neq << 16), &tot);
-    const int eq_before = E + static_cast<int>(ex >> 16);
-    // P counts the ties taken before this chunk (min(E, need)); add the ones taken in
-    // this chunk before this thread.
-    int pos = P + static_cast<int>(ex & 0xffffu) + (min(eq_before, need) - min(E, need));
-    int eq_rank = eq_before;
-#pragma unroll
-    for (int j = 0; j < kVPT; ++j) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const uint32_t kk = key[j][e];
-        bool sel = kk > T;
-        if (kk == T) {
-          sel = eq_rank < need;
-          ++eq_rank;
-        }
-        if (sel) {
-          if (pos < k) out[pos] = (v0 + j) * 8 + e;
-          else raise_status(DCR_ERR_DEVICE_INDEX);
-          ++pos;
-        }
-      }
-    }
-    const int chunk_eq = static_cast<int>(tot >> 16);
-    const int chunk_gt = static_cast<int>(tot & 0xffffu);
-    P += chunk_gt + (min(E + chunk_eq, need) - min(E, need));
-    E += chunk_eq;
+  for (int e = 0; e < kKeys; ++e) {
+    gtm[e >> 5] |= (key[e] > T ? 1u : 0u) << (e & 31);
+    eqm[e >> 5] |= (key[e] == T ? 1u : 0u) << (e & 31);
   }
+  uint32_t ngt = 0, neq = 0;
+#pragma unroll
+  for (int w = 0; w < kWords; ++w) {
+    ngt += __popc(gtm[w]);
+    neq += __popc(eqm[w]);
+  }
+
+  // block exclusive scan of the packed counts (gt in the low 16 bits, eq in the high)
+  const uint32_t packed = ngt | (neq << 16);
+  const uint32_t incl = warp_incl_scan(packed);
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t ws = lane < kP2Warps ? wsum[lane] : 0u;
+    const uint32_t wi = warp_incl_scan(ws);
+    if (lane < kP2Warps) wsum[lane] = wi - ws;
+    if (lane == kP2Warps - 1) scan_tot = wi;
+  }
+  __syncthreads();
+  const uint32_t ex = incl - packed + wsum[warp];
+
+  // ---- exchange the per-CTA totals through CTA 0 -------------------------------------
+  uint32_t gt_before = 0, eq_before_cta = 0;
+  if (C > 1) {
+    if (tid == 0) {
+      gt0[crank] = scan_tot & 0xffffu;
+      eq0[crank] = scan_tot >> 16;
+    }
+    cluster.sync();
+    for (int c = 0; c < crank; ++c) {
+      gt_before += gt0[c];
+      eq_before_cta += eq0[c];
+    }
+  }
+
+  // ---- emission ----------------------------------------------------------------------
+  const int eq_before = static_cast<int>(eq_before_cta + (ex >> 16));
+  int pos = static_cast<int>(gt_before + (ex & 0xffffu)) + min(eq_before, need);
+  int take = need - eq_before;  // ties this thread may take, lowest positions first
+  int32_t* out = p.idx + static_cast<int64_t>(row) * k;
+  const int base = v0 * 8;
+#pragma unroll
+  for (int w = 0; w < kWords; ++w) {
+    uint32_t sel = gtm[w];
+    const uint32_t eq = eqm[w];
+    const int neq_w = __popc(eq);
+    if (take >= neq_w) {
+      sel |= eq;
+      take -= neq_w;
+    } else if (take > 0) {
+      uint32_t rem = eq;
+      for (int i = 0; i < take; ++i) rem &= rem - 1;  // drop the lowest `take` bits
+      sel |= eq & ~rem;
+      take = 0;
+    }
+    while (sel) {
+      const int b = __ffs(sel) - 1;
+      sel &= sel - 1;
+      if (pos < k) out[pos] = base + 32 * w + b;
+      else raise_status(DCR_ERR_DEVICE_INDEX);
+      ++pos;
+    }
+  }
+  if (C > 1) cluster.sync();  // CTA 0's shared memory stays alive until all reads are done
+}
+
+template <int VPT>
+static int launch_select_t(const P2Params& p, int rows, int C, cudaStream_t st) {
+  return launch_cluster(select_kernel<VPT>, dim3(static_cast<unsigned>(rows * C)),
+                        dim3(kP2Threads), 0, st, C, p) == cudaSuccess
+             ? DCR_OK
+             : DCR_ERR_CUDA;
 }
 
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
                   int keys_in, int32_t* idx, int* row_counters, cudaStream_t st) {
   P2Params p;
-  p.keys_in = keys_in;
   p.scores = scores;
   p.stride = s_stride_row;
   p.N = N;
   p.k = k_eff;
   p.idx = idx;
   p.row_counters = row_counters;
+  p.keys_in = keys_in;
   p.vec = ((reinterpret_cast<uintptr_t>(scores) & 15u) == 0 && (s_stride_row & 7) == 0) ? 1 : 0;
-  p.staged = (p.vec && N <= kP2SmemKeys) ? 1 : 0;
-  if (p.staged) {
-    if (ensure_smem_attr(reinterpret_cast<const void*>(&select_kernel<true>), kP2DynSmem) !=
-        cudaSuccess)
-      return DCR_ERR_CUDA;
-    select_kernel<true><<<rows, kP2Threads, kP2DynSmem, st>>>(p);
-  } else {
-    select_kernel<false><<<rows, kP2Threads, 0, st>>>(p);
-  }
-  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+  const int nvec = (N + 7) / 8;
+  // Cluster size: split a row only when the rows alone leave SMs idle or a row is longer
+  // than 32K positions (at most 64 keys per thread).
+  const int64_t sms = device_sm_count();
+  int C = 1;
+  while (C < kP2MaxCluster && static_cast<int64_t>(rows) * (2 * C) <= sms) C *= 2;
+  while (C < kP2MaxCluster && nvec > C * kP2Threads * 8) C *= 2;
+  if (nvec > C * kP2Threads * 8) return DCR_ERR_SHAPE;  // more than 262144 positions per row
+  p.seg_vec = (nvec + C - 1) / C;
+  const int vpt = (p.seg_vec + kP2Threads - 1) / kP2Threads;
+  if (vpt <= 1) return launch_select_t<1>(p, rows, C, st);
+  if (vpt <= 2) return launch_select_t<2>(p, rows, C, st);
+  if (vpt <= 4) return launch_select_t<4>(p, rows, C, st);
+  return launch_select_t<8>(p, rows, C, st);
 }
 
 }  // namespace dcr
