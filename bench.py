@@ -9,10 +9,12 @@ writes 4915). Each step uses a fresh Q and one of 4 distinct layer caches in rot
 seeded inputs with the reference's sink / outlier-channel distribution.
 
 Metric: microseconds per layer-step (lower is better). ``value`` is device time of the
-timed K steps, replayed as one CUDA graph (max over ranks), divided by the steps of all
-ranks; the same K steps launched one by one are reported as ``eager_us_per_step``. With N GPUs every rank
-runs its own shard of (b, h_kv) units of the same size (weak scaling, no collective on the
-data path). Also reported: per-kernel times from CUDA events inside a second, instrumented
+timed K steps, replayed as one CUDA graph (max over ranks), divided by K; the same K
+steps launched one by one are reported as ``eager_us_per_step``. With N GPUs (torchrun,
+one rank per GPU) the layer's context is split by sequence: every GPU holds 32768
+positions of the hero layer, the whole job is a layer-step over 32768 * N positions with
+an exact global top-K (weak scaling; ``--split heads`` splits the 8 KV heads instead).
+Also reported: per-kernel times from CUDA events inside a second, instrumented
 timed loop; the roofline of the dominant kernel against the measured HBM bandwidth; the
 end-to-end time through the public API with host buffers; the CPU baseline (the C oracle,
 a restatement of the reference's algorithm, on the host cores).
@@ -135,11 +137,21 @@ def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s, max_groups=
     return per_layer, threads, len(times), b_sample
 
 
+def _workload_name(world, split):
+    if world == 1:
+        return "config1 hero single-layer decode (fresh Q per step)"
+    if split == "seq":
+        return (f"hero layer with the context split by sequence over {world} GPUs: "
+                f"32768 positions per GPU, N={CFG['N'] * world} in total (weak scaling)")
+    return f"hero layer with its 8 KV heads split over {world} GPUs (strong scaling)"
+
+
 def run_reference_arm(args):
     rank, world, _ = _env()
     if rank != 0:
         return 0
-    B, H, H_kv, N = CFG["B"], CFG["H"], CFG["H_kv"], CFG["N"]
+    B, H, H_kv = CFG["B"], CFG["H"], CFG["H_kv"]
+    N = CFG["N"] * (world if args.split == "seq" else 1)  # the whole job's context
     k = _k_eff(N, CFG["coverage"])
     # each step = one sample (batch row 0) of the layer; value scaled to the full layer
     import torch
@@ -162,14 +174,14 @@ def run_reference_arm(args):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(value / 1e3, 4), "higher_is_better": False,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "config1 hero single-layer decode", "B": B, "N": N, "H": H,
+        "config": {"workload": _workload_name(world, args.split), "B": B, "N": N, "H": H,
                    "H_kv": H_kv, "D": 64, "k_eff": k, "coverage": CFG["coverage"],
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads,
                          "kind": "port",
                          "sample": "C oracle (oracle/dcr_oracle.c, OpenMP) restating "
                                    "topk_qaxis_attention_reference; each step = batch row 0 "
-                                   "(32 q-heads, N=32768) scaled x4 to the B=4 layer"},
+                                   f"(32 q-heads, N={N}) scaled x{B} to the B={B} layer"},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -435,6 +447,216 @@ def run_gpu_arm(args):
     return 0
 
 
+def run_sharded_arm(args):
+    """N > 1: one layer-step over a KV cache split across the ranks (one GPU each).
+
+    --split seq (default): rank r holds positions [32768 r, 32768 (r+1)) of every cache
+    row of the hero layer (B=4, 32/8 heads), so the whole job is a layer-step over an
+    N = 32768 * world context with k_eff = adaptive_k_window(64, N, 0.15); the exact global
+    top-K takes two histogram exchanges and the outputs one (m, l, o) exchange (NCCL).
+    Weak scaling: the per-GPU work stays that of the 1-GPU hero step.
+    --split heads: the hero layer's 8 KV heads split over the ranks and one all-gather of
+    O (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200 import _lib
+    from dcr_b200.sharded import SequenceShardedDecoder, kv_head_sharded_attention
+    from dcr_b200.synthetic import fresh_queries, make_decode_inputs
+
+    rank, world, local = _env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120),
+                            device_id=dev)
+    _lib.load()
+    B, H, H_kv, D = CFG["B"], CFG["H"], CFG["H_kv"], CFG["D"]
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
+    eb = 2
+    steps, warm = args.steps, args.warmup
+    seq = args.split == "seq"
+    if seq:
+        n_local, h_kv_local = CFG["N"], H_kv
+        N = n_local * world
+    else:
+        if H_kv % world:
+            raise SystemExit(f"--split heads needs world dividing H_kv={H_kv}")
+        n_local, h_kv_local = CFG["N"], H_kv // world
+        N = n_local
+    k = _k_eff(N, CFG["coverage"])
+    caches = []
+    for L in range(LAYERS):
+        g = torch.Generator(device=dev).manual_seed(1000 * rank + L)
+        _, K, V = make_decode_inputs(B, H, h_kv_local, n_local, dtype=dt, device=dev,
+                                     generator=g)
+        caches.append((K, V))
+    Qs = fresh_queries(max(steps, warm) + 1, B, H, dtype=dt, seed=7, device=dev)  # replicated
+    O = torch.empty(B, H, D, dtype=dt, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    if seq:
+        dec = SequenceShardedDecoder(B, H, H_kv, n_local, k, dtype=dt, device=dev)
+
+        def step(i):
+            K, V = caches[i % LAYERS]
+            dec(Qs[i % Qs.shape[0]], K, V, out=O)
+    else:
+        from dcr_b200.kernel.cuda._common import workspace_bytes
+        ws = torch.empty(workspace_bytes(B, H // world, h_kv_local, n_local, k),
+                         dtype=torch.uint8, device=dev)
+
+        def local_attn(Qr, Kr, Vr, k_eff, eps=1e-12):
+            from dcr_b200.kernel.cuda import topk_qaxis_attention
+            return topk_qaxis_attention(Qr, Kr, Vr, k_eff, eps=eps, workspace_buf=ws)
+
+        def step(i):
+            K, V = caches[i % LAYERS]
+            O.copy_(kv_head_sharded_attention(Qs[i % Qs.shape[0]], K, V, k,
+                                              local_attention=local_attn))
+
+    def barrier():
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(warm):
+        step(i)
+    barrier()
+    if _lib.read_device_status(clear=True):
+        raise RuntimeError("device status raised during warm-up")
+    gpu_index = dev.index
+    if os.environ.get("CUDA_VISIBLE_DEVICES"):
+        gpu_index = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index])
+    with ClockSampler(gpu_index) as clk:
+        t_soak = time.perf_counter() + args.soak
+        i = 0
+        while time.perf_counter() < t_soak:
+            step(i)
+            i += 1
+            if i % 32 == 0:
+                torch.cuda.synchronize(dev)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        e0.record(stream)
+        for i in range(steps):
+            step(i)
+        e1.record(stream)
+        barrier()
+        ms_eager = e0.elapsed_time(e1)
+        # headline: the same K steps (collectives included) replayed as one CUDA graph
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(cap):
+            with torch.cuda.graph(graph, stream=cap):
+                for i in range(steps):
+                    step(i)
+            graph.replay()
+            barrier()
+            e0.record(cap)
+            graph.replay()
+            e1.record(cap)
+        barrier()
+        ms = e0.elapsed_time(e1)
+        del graph
+    clocks = clk.summary()
+    status = _lib.read_device_status(clear=True)
+
+    # phase breakdown of the sequence split (events on the launching stream)
+    phases = None
+    if seq:
+        from dcr_b200.sharded import sequence_shard_step  # noqa: F401  (same phases, timed)
+        names = ["score", "allreduce_hist_hi", "refine", "allgather_hist_lo", "attend",
+                 "allgather_state", "combine"]
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
+               for _ in range(steps)]
+        comm, st, b = dec.comm, dec.step, dec.bufs
+        barrier()
+        for i in range(steps):
+            K, V = caches[i % LAYERS]
+            st.bind(Qs[i % Qs.shape[0]], K, V)
+            e = evs[i]
+            e[0].record(stream)
+            st.score(b["hist_hi"]); e[1].record(stream)
+            comm.all_reduce_sum_(b["hist_hi"]); e[2].record(stream)
+            st.refine(b["hist_hi"], b["hist_lo"]); e[3].record(stream)
+            comm.all_gather(b["hist_lo"], b["hist_lo_all"]); e[4].record(stream)
+            st.attend(b["hist_lo_all"], world, rank, b["state"]); e[5].record(stream)
+            comm.all_gather(b["state"], b["states"]); e[6].record(stream)
+            st.combine(b["states"], O); e[7].record(stream)
+        barrier()
+        phases = {n: round(statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) * 1e3, 2)
+                  for j, n in enumerate(names)}
+
+    # end to end through the public API: pinned host Q in, O out, host sync per step
+    Qh = Qs[:steps].cpu().pin_memory()
+    Oh = torch.empty(steps, B, H, D, dtype=dt).pin_memory()
+    Qd = torch.empty(B, H, D, dtype=dt, device=dev)
+
+    def e2e_step(i):
+        Qd.copy_(Qh[i], non_blocking=True)
+        K, V = caches[i % LAYERS]
+        if seq:
+            dec(Qd, K, V, out=O)
+        else:
+            O.copy_(kv_head_sharded_attention(Qd, K, V, k, local_attention=local_attn))
+        Oh[i].copy_(O, non_blocking=True)
+        stream.synchronize()
+
+    for i in range(3):
+        e2e_step(i)
+    barrier()
+    f0 = torch.cuda.Event(enable_timing=True)
+    f1 = torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(steps):
+        e2e_step(i)
+    f1.record(stream)
+    barrier()
+    e2e_ms = f0.elapsed_time(f1)
+
+    t = torch.tensor([ms, e2e_ms, ms_eager], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, ms_eager = float(t[0]), float(t[1]), float(t[2])
+    value = ms * 1e3 / steps
+    # our kernels per step; seq: score, 2 histograms, count, emit, attend, combine;
+    # heads: the 3 passes of dcr_decode
+    launches_per_step = 7 if seq else 3
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 5),
+        "higher_is_better": False, "scaling": "weak" if seq else "strong",
+        "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": {"workload": _workload_name(world, args.split), "B": B, "N": N,
+                   "N_per_gpu": n_local, "H": H, "H_kv": H_kv, "H_kv_per_gpu": h_kv_local,
+                   "D": D, "k_eff": k, "coverage": CFG["coverage"],
+                   "parallelism": (f"sequence split over {world} GPUs, exact global top-K "
+                                   "(NCCL all-reduce + 2 all-gathers per layer-step)") if seq
+                   else f"KV-head split over {world} GPUs (NCCL all-gather of O)",
+                   "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
+                         f"{2 * B * h_kv_local * n_local * D * eb / 1e6:.0f} MB per GPU",
+                   "launch": "the K timed steps (collectives included) replayed as one CUDA "
+                             "graph",
+                   "eager_us_per_step": round(ms_eager * 1e3 / steps, 3),
+                   "clock_soak_s": args.soak},
+        "phases_us": phases,
+        "cpu_baseline": None,
+        "e2e": {"value": round(e2e_ms * 1e3 / steps, 3), "unit": UNIT,
+                "h2d_bytes_per_step": B * H * D * eb, "d2h_bytes_per_step": B * H * D * eb,
+                "api": ("dcr_b200.sharded.SequenceShardedDecoder" if seq
+                        else "dcr_b200.sharded.kv_head_sharded_attention") +
+                       ", pinned host Q in / O out on every rank, host sync per step"},
+        "gpu_launches": launches_per_step * steps,
+        "device_status": status,
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -444,6 +666,9 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5, help="untimed seconds before timing")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--split", choices=["seq", "heads"], default="seq",
+                    help="multi-GPU layout: context split by sequence (weak scaling, exact "
+                         "global top-K) or KV heads split (strong scaling)")
     ap.add_argument("--dtype", choices=["f16", "bf16"], default=CFG["dtype"],
                     help="cache/query dtype (config 1 is fp16)")
     args = ap.parse_args()
@@ -451,6 +676,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_sharded_arm(args)
     return run_gpu_arm(args)
 
 

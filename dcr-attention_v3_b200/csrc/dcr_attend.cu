@@ -56,9 +56,11 @@ struct P3Params {
   const void* k;
   const void* v;
   int64_t ksb, ksh, vsb, vsh;  // element strides
-  const int32_t* idx;
+  const int32_t* idx;       // [rows][k_eff]: row r's list starts at r * k_eff
+  const int32_t* counts;    // optional [rows]: row r uses its first counts[r] entries
   int H, H_kv, G, N, k_eff, S;
-  void* o;
+  void* o;                  // [rows][D] output (when state == nullptr)
+  float* state;             // optional [rows][D + 2]: (m, l, o) instead of O
   float* part;
   int* counters;
 };
@@ -95,8 +97,10 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   const int h = hk * p.G + j;
   const int64_t row = static_cast<int64_t>(b) * p.H + h;
 
-  const int64_t p0 = static_cast<int64_t>(s) * p.k_eff / p.S;
-  const int64_t p1 = static_cast<int64_t>(s + 1) * p.k_eff / p.S;
+  int row_k = p.k_eff;
+  if (p.counts != nullptr) row_k = min(max(__ldg(p.counts + row), 0), p.k_eff);
+  const int64_t p0 = static_cast<int64_t>(s) * row_k / p.S;
+  const int64_t p1 = static_cast<int64_t>(s + 1) * row_k / p.S;
   const int cnt = static_cast<int>(p1 - p0);
   const int ntiles = (cnt + kP3Tile - 1) / kP3Tile;
   const int32_t* idx_row = p.idx + row * p.k_eff + p0;
@@ -280,7 +284,16 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   }
 
   if (p.S == 1) {
-    if (tid < kD) ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / l_cta);
+    if (p.state != nullptr) {
+      float* st = p.state + row * (kD + 2);
+      if (tid < kD) st[2 + tid] = od;
+      if (tid == 0) {
+        st[0] = M;
+        st[1] = l_cta;
+      }
+    } else if (tid < kD) {
+      ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / l_cta);
+    }
     return;
   }
 
@@ -308,7 +321,16 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
       L = fmaf(w, __ldcg(pt + 1), L);
       o = fmaf(w, __ldcg(pt + 2 + tid), o);
     }
-    ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), o / L);
+    if (p.state != nullptr) {
+      float* st = p.state + row * (kD + 2);
+      st[2 + tid] = o;
+      if (tid == 0) {
+        st[0] = Mg;
+        st[1] = L;
+      }
+    } else {
+      ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), o / L);
+    }
   }
   if (tid == 0) p.counters[row] = 0;
 }
@@ -336,8 +358,9 @@ static int launch_attend_t(const P3Params& p, int B, cudaStream_t st) {
 
 int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
                   int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,
-                  const int32_t* idx, int B, int H, int H_kv, int N, int k_eff, void* O,
-                  int splits, float* partials, int* counters, cudaStream_t st) {
+                  const int32_t* idx, const int32_t* counts, int B, int H, int H_kv, int N,
+                  int k_eff, void* O, float* state, int splits, float* partials, int* counters,
+                  cudaStream_t st) {
   P3Params p;
   p.q = Q;
   p.k = K;
@@ -347,6 +370,7 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
   p.vsb = v_stride_b;
   p.vsh = v_stride_h;
   p.idx = idx;
+  p.counts = counts;
   p.H = H;
   p.H_kv = H_kv;
   p.G = H / H_kv;
@@ -354,6 +378,7 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
   p.k_eff = k_eff;
   p.S = splits;
   p.o = O;
+  p.state = state;
   p.part = partials;
   p.counters = counters;
   switch (dtype) {

@@ -4,5 +4,6 @@
 #include "dcr_score.cu"
 #include "dcr_select.cu"
 #include "dcr_attend.cu"
+#include "dcr_shard.cu"
 #include "dcr_capi.cu"
 #include "dcr_noalloc.cu"

@@ -135,6 +135,8 @@ const char* dcr_status_string(int status) {
     case DCR_ERR_NOALLOC_LIMIT:
       return "shape needs more scratch than dcr_decode_noalloc's 16 MiB array; use dcr_decode";
     case DCR_ERR_DEVICE_INDEX: return "device: an index outside [0, N) was skipped";
+    case DCR_ERR_DEVICE_SHARD:
+      return "device: sharded selection saw inconsistent global histograms (k_eff >= total N?)";
     default: return "unknown status";
   }
 }
@@ -208,13 +210,16 @@ int dcr_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k
   int* counters = nullptr;
   if (w.splits > 1) {
     if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return DCR_ERR_ALIGN;
+  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     partials = reinterpret_cast<float*>(ws + w.partials);
     counters = reinterpret_cast<int*>(ws + w.counters);
     if (cudaMemsetAsync(counters, 0, sizeof(int) * rows, s) != cudaSuccess) return DCR_ERR_CUDA;
   }
-  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B,
-                       H, H_kv, N, k_eff, O, w.splits, partials, counters, s);
+  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx,
+                       nullptr, B, H, H_kv, N, k_eff, O, nullptr, w.splits, partials, counters,
+                       s);
 }
 
 int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride_b,
@@ -230,6 +235,7 @@ int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride
   const int rows = B * H;
   const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
   if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -254,6 +260,7 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   const int rows = B * H;
   const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
   if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
   int32_t* idx = reinterpret_cast<int32_t*>(ws + w.idx);
@@ -274,8 +281,9 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   // Pass 2 also resets the Pass 3 split-K tickets of its row.
   if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s))) return st;
   if ((st = mark(2))) return st;
-  if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx, B,
-                          H, H_kv, N, k_eff, O, w.splits, partials, counters, s)))
+  if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx,
+                          nullptr, B, H, H_kv, N, k_eff, O, nullptr, w.splits, partials,
+                          counters, s)))
     return st;
   return mark(3);
 }
@@ -297,6 +305,114 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype, int
     if (events[i] == nullptr) return DCR_ERR_NULL;
   return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
                      N, D, k_eff, eps, O, workspace, workspace_bytes, stream, events);
+}
+
+// ---- sequence-sharded decode ----------------------------------------------------------
+
+size_t dcr_shard_workspace_bytes(int B, int H, int H_kv, int N_local, int D, int k_eff) {
+  if (check_heads(B, H, H_kv, N_local, D) != DCR_OK || k_eff <= 0) return 0;
+  return shard_layout(B * H, N_local, k_eff).total;
+}
+
+static int shard_ws(int B, int H, int N_local, int k_eff, void* workspace,
+                    size_t workspace_bytes, ShardLayout& w) {
+  if (k_eff <= 0) return DCR_ERR_K_RANGE;
+  w = shard_layout(B * H, N_local, k_eff);
+  if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
+  return DCR_OK;
+}
+
+static bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
+
+int dcr_shard_score(const void* Q, const void* K, int dtype, int64_t k_stride_b,
+                    int64_t k_stride_h, int B, int H, int H_kv, int N_local, int D, int k_eff,
+                    float eps, int32_t* hist_hi, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int st = check_heads(B, H, H_kv, N_local, D);
+  if (st) return st;
+  if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N_local))) return st;
+  if (Q == nullptr || hist_hi == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q) || !aligned4(hist_hi)) return DCR_ERR_ALIGN;
+  ShardLayout w;
+  if ((st = shard_ws(B, H, N_local, k_eff, workspace, workspace_bytes, w))) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N_local,
+                         reinterpret_cast<uint16_t*>(ws + w.scores), w.n_pad, 1, s)))
+    return st;
+  return launch_shard_hist(w, ws, B * H, N_local, k_eff, 0, nullptr, hist_hi, s);
+}
+
+int dcr_shard_refine(int B, int H, int H_kv, int N_local, int D, int k_eff,
+                     const int32_t* hist_hi_sum, int32_t* hist_lo, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  int st = check_heads(B, H, H_kv, N_local, D);
+  if (st) return st;
+  if (hist_hi_sum == nullptr || hist_lo == nullptr) return DCR_ERR_NULL;
+  if (!aligned4(hist_hi_sum) || !aligned4(hist_lo)) return DCR_ERR_ALIGN;
+  ShardLayout w;
+  if ((st = shard_ws(B, H, N_local, k_eff, workspace, workspace_bytes, w))) return st;
+  return launch_shard_hist(w, static_cast<uint8_t*>(workspace), B * H, N_local, k_eff, 1,
+                           hist_hi_sum, hist_lo, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_shard_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
+                     int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, int B, int H,
+                     int H_kv, int N_local, int D, int k_eff, const int32_t* hist_lo_all,
+                     int world, int rank, float* state, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  int st = check_heads(B, H, H_kv, N_local, D);
+  if (st) return st;
+  if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N_local))) return st;
+  if ((st = check_cache(V, dtype, v_stride_b, v_stride_h, B, H_kv, N_local))) return st;
+  if (Q == nullptr || hist_lo_all == nullptr || state == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q) || !aligned4(hist_lo_all) || !aligned4(state)) return DCR_ERR_ALIGN;
+  if (world <= 0 || rank < 0 || rank >= world) return DCR_ERR_SHAPE;
+  ShardLayout w;
+  if ((st = shard_ws(B, H, N_local, k_eff, workspace, workspace_bytes, w))) return st;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int rows = B * H;
+  // the selection also resets the Pass 3 tickets
+  if ((st = launch_shard_select(w, ws, rows, N_local, k_eff, hist_lo_all, world, rank, s)))
+    return st;
+  return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+                       reinterpret_cast<const int32_t*>(ws + w.idx),
+                       reinterpret_cast<const int32_t*>(ws + w.count), B, H, H_kv, N_local,
+                       w.cap, nullptr, state, w.splits, reinterpret_cast<float*>(ws + w.partials),
+                       reinterpret_cast<int*>(ws + w.counters), s);
+}
+
+int dcr_shard_combine(const float* states, int world, int B, int H, int D, int dtype, void* O,
+                      void* stream) {
+  if (states == nullptr || O == nullptr) return DCR_ERR_NULL;
+  if (B <= 0 || H <= 0 || D != kD || world <= 0) return DCR_ERR_SHAPE;
+  if (static_cast<int64_t>(B) * H * kD > 0x7fffffffLL) return DCR_ERR_SHAPE;
+  if (dtype_bytes(dtype) == 0) return DCR_ERR_DTYPE;
+  if (!aligned4(states) || !aligned16(O)) return DCR_ERR_ALIGN;
+  return launch_shard_combine(states, world, B * H, dtype, O, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, int H, int H_kv,
+                        int N_local, int D, int k_eff, int32_t* idx_out, int32_t* count_out,
+                        void* stream) {
+  int st = check_heads(B, H, H_kv, N_local, D);
+  if (st) return st;
+  if (idx_out == nullptr || count_out == nullptr) return DCR_ERR_NULL;
+  ShardLayout w;
+  if ((st = shard_ws(B, H, N_local, k_eff, const_cast<void*>(workspace), workspace_bytes, w)))
+    return st;
+  const uint8_t* ws = static_cast<const uint8_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t rows = static_cast<size_t>(B) * H;
+  if (cudaMemcpyAsync(idx_out, ws + w.idx, sizeof(int32_t) * rows * w.cap,
+                      cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  if (cudaMemcpyAsync(count_out, ws + w.count, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice,
+                      s) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  return DCR_OK;
 }
 
 int dcr_read_device_status(int* status_out, int clear) {

@@ -62,9 +62,39 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
                   int keys_in, int32_t* idx, int* row_counters, cudaStream_t st);
 
+// counts (optional): row r attends to the first counts[r] of its k_eff index slots.
+// state (optional): write the unnormalised (m, l, o[D]) per row (m in base-2 units of
+// the scaled scores) instead of O.
 int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
                   int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,
-                  const int32_t* idx, int B, int H, int H_kv, int N, int k_eff, void* O,
-                  int splits, float* partials, int* counters, cudaStream_t st);
+                  const int32_t* idx, const int32_t* counts, int B, int H, int H_kv, int N,
+                  int k_eff, void* O, float* state, int splits, float* partials, int* counters,
+                  cudaStream_t st);
+
+// Workspace layout of the sequence-sharded step (dcr_shard_*): a dcr_decode layout for
+// the local chunk plus the selection's bookkeeping.
+struct ShardLayout {
+  size_t counters;   // int32 [rows] Pass 3 split-K tickets
+  size_t partials;   // fp32 [rows * splits * (D + 2)]
+  size_t scores;     // uint16 [rows * n_pad] order keys of the local chunk
+  size_t idx;        // int32 [rows * cap] selected local positions
+  size_t count;      // int32 [rows]
+  size_t row_state;  // int32 [rows * 4]
+  size_t chunk_cnt;  // uint32 [rows * chunks]
+  size_t total;
+  int splits, cap, chunks;
+  int64_t n_pad;
+};
+ShardLayout shard_layout(int rows, int N_local, int k_eff);
+
+// level 0: high-byte histogram of the local keys; level 1: low-byte histogram of the keys
+// in the bin that hist_hi_sum (summed over ranks) puts the k-th largest key in.
+int launch_shard_hist(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
+                      int level, const int32_t* hist_hi_sum, int32_t* hist_out, cudaStream_t st);
+// This rank's selected positions (ascending) and counts from all ranks' low-byte histograms.
+int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
+                        const int32_t* hist_lo_all, int world, int rank, cudaStream_t st);
+int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
+                         cudaStream_t st);
 
 }  // namespace dcr

@@ -58,52 +58,6 @@ __device__ __forceinline__ uint32_t order_key_fast(uint32_t x) {
   return mag > 0x7f80u ? 0xffffu : key;
 }
 
-__device__ __forceinline__ uint32_t warp_incl_scan(uint32_t x) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, x, off);
-    if (lane >= off) x += y;
-  }
-  return x;
-}
-
-// One warp finds, in a 256-bin histogram h, the bin B with #{above B} < k <= #{above B-1}
-// (counting from the top) and returns B and above = #{keys in bins above B}.
-__device__ __forceinline__ void warp_find_bin(const uint32_t* h, uint32_t k, int& bin,
-                                              uint32_t& above) {
-  const int lane = threadIdx.x & 31;
-  uint32_t c[8];
-  uint32_t tot = 0;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    c[i] = h[8 * lane + i];
-    tot += c[i];
-  }
-  // inclusive suffix sum over lanes: sum of tot over lanes >= lane
-  uint32_t suf = tot;
-#pragma unroll
-  for (int off = 1; off < 32; off <<= 1) {
-    const uint32_t y = __shfl_down_sync(0xffffffffu, suf, off);
-    if (lane + off < 32) suf += y;
-  }
-  uint32_t a = suf - tot;  // keys in bins above this lane's 8 bins
-  int found = -1;
-  uint32_t found_above = 0;
-#pragma unroll
-  for (int i = 7; i >= 0; --i) {
-    if (found < 0 && a < k && k <= a + c[i]) {
-      found = 8 * lane + i;
-      found_above = a;
-    }
-    a += c[i];
-  }
-  const unsigned m = __ballot_sync(0xffffffffu, found >= 0);
-  const int src = m ? (__ffs(m) - 1) : 0;
-  bin = __shfl_sync(0xffffffffu, found, src);
-  above = __shfl_sync(0xffffffffu, found_above, src);
-}
-
 // VPT: vectors (8 positions each) per thread, 1..8.
 template <int VPT>
 __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p) {

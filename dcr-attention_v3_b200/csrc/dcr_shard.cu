@@ -1,0 +1,378 @@
+// dcr_shard.cu — sequence-sharded decode: the exact global top-K over KV-cache chunks held
+// by several GPUs, and the cross-GPU (m, l, o) combine.
+//
+// The reference's decode path runs on one GPU; this file has no counterpart there. The
+// set it selects is the reference's (_select_topk_indices,
+// dcr_attention/kernel/qaxis_topk_reference.py:91: stable descending argsort of the
+// scores over the whole context, first k_eff) taken over the concatenation of the ranks'
+// chunks in rank order, and the attention is _fused_softmax_attention (:148) over that
+// set, computed piecewise by rank and merged exactly.
+//
+// Rank r holds positions [off_r, off_r + N_r) of every (b, h_kv) cache, off_r increasing
+// with r. One decode step is four phases separated by three collectives that the caller
+// runs (NCCL over NVLink in dcr_b200.sharded):
+//   1. dcr_shard_score: Pass 1 over the local chunk (16-bit order keys into the
+//      workspace) and, per row, a 256-bin histogram of the keys' high byte.
+//                                                      -> all-reduce (sum) of [rows][256]
+//   2. dcr_shard_refine: from the global high-byte histogram, the bin BH that holds the
+//      k-th largest key; a 256-bin histogram of the low byte of the local keys in BH.
+//                                                      -> all-gather into [world][rows][256]
+//   3. dcr_shard_attend: the summed low-byte histograms give T (the k-th largest key) and
+//      need = k_eff - #{key > T} over all ranks. Keys equal to T are taken in position
+//      order, and lower ranks hold lower positions, so rank r takes
+//          quota_r = clamp(need - #{key == T on ranks < r}, 0, #{key == T on rank r}).
+//      The rank lists its positions with key > T and its first quota_r positions with
+//      key == T, ascending, and runs Pass 3 over them, writing the unnormalised state
+//      (m, l, o[64]) of every row instead of O.       -> all-gather into [world][rows][66]
+//   4. dcr_shard_combine: O = sum_r 2^{m_r - M} o_r / sum_r 2^{m_r - M} l_r, M = max_r m_r.
+//
+// Phase kernels (B200): a CTA of 256 threads takes an 8192-position chunk of one row, 32
+// contiguous keys per thread read as four 16-byte loads (the keys were just written by
+// Pass 1 and are served from L2). Histograms use shared-memory atomics and add their
+// non-zero bins into the row's global histogram. Listing the selection takes two
+// launches: per-chunk counts of (key > T, key == T), then each chunk's output offset
+// from the counts of the chunks before it and a block-wide scan inside the chunk.
+#include "dcr_common.cuh"
+#include "dcr_internal.h"
+
+namespace dcr {
+
+constexpr int kShThreads = 256;
+constexpr int kShWarps = kShThreads / 32;
+constexpr int kShKeys = 32;                     // contiguous keys per thread
+constexpr int kShChunk = kShThreads * kShKeys;  // positions per CTA
+constexpr int kShStateFloats = kD + 2;          // (m, l, o[64])
+
+struct ShardParams {
+  const uint16_t* keys;       // order keys (Pass 1 keys_out), rows n_pad apart
+  int64_t stride;
+  int rows, N, k, chunks, cap, world, rank;
+  const int32_t* hist_hi;     // [rows][256] summed over ranks (phase 2)
+  const int32_t* hist_lo_all; // [world][rows][256] (phase 3)
+  int32_t* hist_out;          // [rows][256] this rank's histogram (phases 1, 2)
+  int32_t* row_state;         // [rows][4]: BH, #{key above bin BH}, T, quota
+  uint32_t* chunk_cnt;        // [rows][chunks]: #{key > T} | #{key == T} << 16
+  int32_t* idx;               // [rows][cap] selected local positions, ascending
+  int32_t* count;             // [rows] number of selected local positions
+  int* counters;              // Pass 3 split-K tickets, reset by phase 3
+};
+
+// The 32 keys of this thread in chunk `chunk` of row `row`; 0 past the end of the row
+// (no real score maps to key 0: the lowest real key is that of -inf, 0x007f).
+__device__ __forceinline__ void shard_load_keys(const ShardParams& p, int64_t row, int chunk,
+                                                uint32_t (&key)[kShKeys]) {
+  const uint16_t* src = p.keys + row * p.stride;
+  const int64_t base = static_cast<int64_t>(chunk) * kShChunk +
+                       static_cast<int64_t>(threadIdx.x) * kShKeys;
+  if (base + kShKeys <= p.N) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + base);
+#pragma unroll
+    for (int j = 0; j < kShKeys / 8; ++j) {
+      const uint4 w = __ldcg(s4 + j);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        key[8 * j + 2 * i] = ww[i] & 0xffffu;
+        key[8 * j + 2 * i + 1] = ww[i] >> 16;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < kShKeys; ++e) key[e] = (base + e < p.N) ? src[base + e] : 0u;
+  }
+}
+
+// Phase 1 (kLevel 0): histogram of key >> 8. Phase 2 (kLevel 1): find BH in the global
+// high-byte histogram, then histogram key & 0xff over the keys in BH.
+template <int kLevel>
+__global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParams p) {
+  __shared__ uint32_t h[256];
+  __shared__ uint32_t s_bh;
+  const int tid = threadIdx.x;
+  const int64_t row = blockIdx.x / p.chunks;
+  const int chunk = blockIdx.x % p.chunks;
+  h[tid] = 0u;
+  if (kLevel == 1 && tid < 32) {
+    int bin;
+    uint32_t above;
+    warp_find_bin(reinterpret_cast<const uint32_t*>(p.hist_hi + row * 256),
+                  static_cast<uint32_t>(p.k), bin, above);
+    if (tid == 0) {
+      if (bin < 0) {  // fewer than k keys over all ranks
+        raise_status(DCR_ERR_DEVICE_SHARD);
+        bin = 0;
+        above = 0;
+      }
+      s_bh = static_cast<uint32_t>(bin);
+      if (chunk == 0) {
+        p.row_state[row * 4 + 0] = bin;
+        p.row_state[row * 4 + 1] = static_cast<int32_t>(above);
+      }
+    }
+  }
+  uint32_t key[kShKeys];
+  shard_load_keys(p, row, chunk, key);
+  __syncthreads();
+  if (kLevel == 0) {
+#pragma unroll
+    for (int e = 0; e < kShKeys; ++e)
+      if (key[e] != 0u) atomicAdd(&h[key[e] >> 8], 1u);
+  } else {
+    const uint32_t bh = s_bh;
+#pragma unroll
+    for (int e = 0; e < kShKeys; ++e)
+      if (key[e] != 0u && (key[e] >> 8) == bh) atomicAdd(&h[key[e] & 0xffu], 1u);
+  }
+  __syncthreads();
+  const uint32_t c = h[tid];
+  if (c) atomicAdd(reinterpret_cast<unsigned int*>(p.hist_out + row * 256 + tid), c);
+}
+
+// Phase 3a: T and this rank's tie quota from the gathered low-byte histograms; per-chunk
+// counts of keys > T and == T.
+__global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardParams p) {
+  __shared__ uint32_t h[256];
+  __shared__ uint32_t s_T;
+  __shared__ uint32_t red[kShWarps];
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t row = blockIdx.x / p.chunks;
+  const int chunk = blockIdx.x % p.chunks;
+  const uint32_t bh = static_cast<uint32_t>(p.row_state[row * 4 + 0]);
+  const uint32_t above = static_cast<uint32_t>(p.row_state[row * 4 + 1]);
+  uint32_t tot = 0;
+  for (int r = 0; r < p.world; ++r)
+    tot += static_cast<uint32_t>(p.hist_lo_all[(static_cast<int64_t>(r) * p.rows + row) * 256 + tid]);
+  h[tid] = tot;
+  uint32_t key[kShKeys];
+  shard_load_keys(p, row, chunk, key);
+  __syncthreads();
+  if (warp == 0) {
+    int bl;
+    uint32_t above_lo;
+    warp_find_bin(h, static_cast<uint32_t>(p.k) - above, bl, above_lo);
+    if (lane == 0) {
+      if (bl < 0) {
+        raise_status(DCR_ERR_DEVICE_SHARD);
+        bl = 0;
+        above_lo = 0;
+      }
+      const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
+      const int need = p.k - static_cast<int>(above + above_lo);
+      int eq_lower = 0;
+      for (int r = 0; r < p.rank; ++r)
+        eq_lower += p.hist_lo_all[(static_cast<int64_t>(r) * p.rows + row) * 256 + bl];
+      const int eq_mine = p.hist_lo_all[(static_cast<int64_t>(p.rank) * p.rows + row) * 256 + bl];
+      const int quota = max(0, min(need - eq_lower, eq_mine));
+      s_T = T;
+      if (chunk == 0) {
+        p.row_state[row * 4 + 2] = static_cast<int32_t>(T);
+        p.row_state[row * 4 + 3] = quota;
+      }
+    }
+  }
+  __syncthreads();
+  const uint32_t T = s_T;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int e = 0; e < kShKeys; ++e) packed += (key[e] > T) ? 1u : ((key[e] == T) ? 0x10000u : 0u);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) packed += __shfl_xor_sync(0xffffffffu, packed, off);
+  if (lane == 0) red[warp] = packed;
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t s = 0;
+#pragma unroll
+    for (int w = 0; w < kShWarps; ++w) s += red[w];
+    p.chunk_cnt[row * p.chunks + chunk] = s;
+  }
+}
+
+// Phase 3b: list the selected local positions of the chunk, ascending.
+__global__ void __launch_bounds__(kShThreads) shard_emit_kernel(const ShardParams p) {
+  __shared__ uint32_t wsum[kShWarps];
+  __shared__ uint32_t s_gt_before, s_eq_before, s_gt_all;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t row = blockIdx.x / p.chunks;
+  const int chunk = blockIdx.x % p.chunks;
+  const uint32_t T = static_cast<uint32_t>(p.row_state[row * 4 + 2]);
+  const uint32_t quota = static_cast<uint32_t>(p.row_state[row * 4 + 3]);
+  if (warp == 0) {
+    uint32_t gb = 0, eb = 0, ga = 0;
+    for (int c = lane; c < p.chunks; c += 32) {
+      const uint32_t v = p.chunk_cnt[row * p.chunks + c];
+      ga += v & 0xffffu;
+      if (c < chunk) {
+        gb += v & 0xffffu;
+        eb += v >> 16;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      gb += __shfl_xor_sync(0xffffffffu, gb, off);
+      eb += __shfl_xor_sync(0xffffffffu, eb, off);
+      ga += __shfl_xor_sync(0xffffffffu, ga, off);
+    }
+    if (lane == 0) {
+      s_gt_before = gb;
+      s_eq_before = eb;
+      s_gt_all = ga;
+    }
+  }
+  uint32_t key[kShKeys];
+  shard_load_keys(p, row, chunk, key);
+  uint32_t packed = 0;
+#pragma unroll
+  for (int e = 0; e < kShKeys; ++e) packed += (key[e] > T) ? 1u : ((key[e] == T) ? 0x10000u : 0u);
+  const uint32_t incl = warp_incl_scan(packed);
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t ws = lane < kShWarps ? wsum[lane] : 0u;
+    const uint32_t wi = warp_incl_scan(ws);
+    if (lane < kShWarps) wsum[lane] = wi - ws;
+  }
+  __syncthreads();
+  const uint32_t ex = incl - packed + wsum[warp];
+  uint32_t eq_rank = s_eq_before + (ex >> 16);  // ties on this rank before this thread's keys
+  int64_t pos = static_cast<int64_t>(s_gt_before) + (ex & 0xffffu) + min(eq_rank, quota);
+  int32_t* out = p.idx + row * p.cap;
+  const int base = chunk * kShChunk + tid * kShKeys;
+#pragma unroll
+  for (int e = 0; e < kShKeys; ++e) {
+    bool take = key[e] > T;
+    if (key[e] == T) {
+      take = eq_rank < quota;
+      ++eq_rank;
+    }
+    if (take) {
+      if (pos < p.cap) {
+        out[pos] = base + e;
+      } else {
+        raise_status(DCR_ERR_DEVICE_SHARD);
+      }
+      ++pos;
+    }
+  }
+  if (chunk == 0 && tid == 0) {
+    p.count[row] = static_cast<int32_t>(min(s_gt_all + quota, static_cast<uint32_t>(p.cap)));
+    p.counters[row] = 0;
+  }
+}
+
+// Phase 4: merge the ranks' (m, l, o) states of a row into O.
+template <typename T>
+__global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, int world,
+                                                           int rows, void* O) {
+  const int64_t row = blockIdx.x;
+  const int tid = threadIdx.x;
+  float M = -INFINITY;
+  for (int r = 0; r < world; ++r)
+    M = fmaxf(M, states[(static_cast<int64_t>(r) * rows + row) * kShStateFloats]);
+  float L = 0.0f, o = 0.0f;
+  for (int r = 0; r < world; ++r) {
+    const float* st = states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats;
+    const float m = st[0];
+    const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+    L = fmaf(w, st[1], L);
+    o = fmaf(w, st[2 + tid], o);
+  }
+  ElemTraits<T>::store(O, static_cast<int>(row * kD + tid), o / L);
+}
+
+size_t align_up_256(size_t x) { return (x + 255) / 256 * 256; }
+
+ShardLayout shard_layout(int rows, int N_local, int k_eff) {
+  ShardLayout w;
+  w.cap = k_eff < N_local ? k_eff : N_local;
+  w.splits = attend_splits(rows, w.cap);
+  w.n_pad = (static_cast<int64_t>(N_local) + 7) / 8 * 8;
+  w.chunks = static_cast<int>((static_cast<int64_t>(N_local) + kShChunk - 1) / kShChunk);
+  size_t off = 0;
+  w.counters = off;
+  off = align_up_256(off + sizeof(int) * static_cast<size_t>(rows));
+  w.partials = off;
+  off = align_up_256(off + sizeof(float) * static_cast<size_t>(rows) * w.splits * (kD + 2));
+  w.scores = off;
+  off = align_up_256(off + sizeof(uint16_t) * static_cast<size_t>(rows) * w.n_pad);
+  w.idx = off;
+  off = align_up_256(off + sizeof(int32_t) * static_cast<size_t>(rows) * w.cap);
+  w.count = off;
+  off = align_up_256(off + sizeof(int32_t) * static_cast<size_t>(rows));
+  w.row_state = off;
+  off = align_up_256(off + sizeof(int32_t) * 4 * static_cast<size_t>(rows));
+  w.chunk_cnt = off;
+  off = align_up_256(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.chunks);
+  w.total = off;
+  return w;
+}
+
+static ShardParams shard_params(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
+                                int k_eff) {
+  ShardParams p = {};
+  p.keys = reinterpret_cast<const uint16_t*>(ws + w.scores);
+  p.stride = w.n_pad;
+  p.rows = rows;
+  p.N = N_local;
+  p.k = k_eff;
+  p.chunks = w.chunks;
+  p.cap = w.cap;
+  p.row_state = reinterpret_cast<int32_t*>(ws + w.row_state);
+  p.chunk_cnt = reinterpret_cast<uint32_t*>(ws + w.chunk_cnt);
+  p.idx = reinterpret_cast<int32_t*>(ws + w.idx);
+  p.count = reinterpret_cast<int32_t*>(ws + w.count);
+  p.counters = reinterpret_cast<int*>(ws + w.counters);
+  return p;
+}
+
+static int check_launch() { return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA; }
+
+int launch_shard_hist(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
+                      int level, const int32_t* hist_hi_sum, int32_t* hist_out, cudaStream_t st) {
+  ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
+  p.hist_hi = hist_hi_sum;
+  p.hist_out = hist_out;
+  if (cudaMemsetAsync(hist_out, 0, sizeof(int32_t) * 256 * static_cast<size_t>(rows), st) !=
+      cudaSuccess)
+    return DCR_ERR_CUDA;
+  const int64_t grid = static_cast<int64_t>(rows) * w.chunks;
+  if (grid > 0x7fffffff) return DCR_ERR_SHAPE;
+  if (level == 0)
+    shard_hist_kernel<0><<<static_cast<unsigned>(grid), kShThreads, 0, st>>>(p);
+  else
+    shard_hist_kernel<1><<<static_cast<unsigned>(grid), kShThreads, 0, st>>>(p);
+  return check_launch();
+}
+
+int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
+                        const int32_t* hist_lo_all, int world, int rank, cudaStream_t st) {
+  ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
+  p.hist_lo_all = hist_lo_all;
+  p.world = world;
+  p.rank = rank;
+  const int64_t grid = static_cast<int64_t>(rows) * w.chunks;
+  if (grid > 0x7fffffff) return DCR_ERR_SHAPE;
+  shard_count_kernel<<<static_cast<unsigned>(grid), kShThreads, 0, st>>>(p);
+  int e = check_launch();
+  if (e) return e;
+  shard_emit_kernel<<<static_cast<unsigned>(grid), kShThreads, 0, st>>>(p);
+  return check_launch();
+}
+
+int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
+                         cudaStream_t st) {
+  switch (dtype) {
+    case DCR_DTYPE_BF16:
+      shard_combine_kernel<__nv_bfloat16><<<rows, kD, 0, st>>>(states, world, rows, O);
+      break;
+    case DCR_DTYPE_F16: shard_combine_kernel<__half><<<rows, kD, 0, st>>>(states, world, rows, O); break;
+    case DCR_DTYPE_F32: shard_combine_kernel<float><<<rows, kD, 0, st>>>(states, world, rows, O); break;
+    default: return DCR_ERR_DTYPE;
+  }
+  return check_launch();
+}
+
+}  // namespace dcr

@@ -27,6 +27,7 @@ DCR_ERR_CUDA = 7
 DCR_ERR_DEVICE_TIMEOUT = 8
 DCR_ERR_NOALLOC_LIMIT = 9
 DCR_ERR_DEVICE_INDEX = 16
+DCR_ERR_DEVICE_SHARD = 32
 
 # Every exported symbol with its (restype, argtypes); tests check this list against the
 # header and the library's dynamic symbol table.
@@ -52,6 +53,15 @@ SIGNATURES = {
     "dcr_decode_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                                 _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp,
                                 ctypes.POINTER(_vp)]),
+    "dcr_shard_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
+    "dcr_shard_score": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,
+                               _f32, _vp, _vp, _sz, _vp]),
+    "dcr_shard_refine": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp, _vp, _sz, _vp]),
+    "dcr_shard_attend": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
+                                _i32, _i32, _i32, _vp, _i32, _i32, _vp, _vp, _sz, _vp]),
+    "dcr_shard_combine": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "dcr_shard_selection": (_i32, [_vp, _sz, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
+                                   _vp]),
     "dcr_read_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
 }
 

@@ -1,0 +1,266 @@
+"""Sparse decode attention over a KV cache split across the GPUs of one node.
+
+The reference runs a layer's decode step on one GPU (topk_qaxis_attention,
+dcr_attention/kernel/triton/topk_axis.py:58). Two splits across ranks keep its result:
+
+* **KV-head split** (:func:`kv_head_sharded_attention`). Rank r of W owns KV heads
+  [r*H_kv/W, (r+1)*H_kv/W) and the query heads that read them. The (b, h_kv) units are
+  independent, so every rank runs the single-GPU step on its heads and one all-gather of
+  the outputs ([B, H/W, D] per rank) assembles O. The selection is the single-GPU one;
+  O differs from it only by fp32 summation order (Pass 3's split-K factor follows the
+  number of rows a GPU holds).
+
+* **Sequence split** (:class:`SequenceShardedDecoder`). Rank r holds positions
+  [off_r, off_r + N_r) of every cache row, off_r increasing with r. The top-K is exact
+  over the whole context: ranks exchange 256-bin histograms of the 16-bit score keys
+  (all-reduce of the high byte, all-gather of the low byte within the threshold's bin),
+  which fixes the k-th largest key T, how many keys above it there are, and, because
+  lower ranks hold lower positions, how many of the keys equal to T each rank takes (the
+  reference's lowest-index tie rule). Each rank attends to its share and publishes its
+  unnormalised (m, l, o); an all-gather and a combine give O. The selected set is the
+  reference's (_select_topk_indices, qaxis_topk_reference.py:91) over the concatenated
+  context; O differs from a single-GPU step only by fp32 summation order.
+
+Collectives go through a :class:`TorchComm` (``torch.distributed``; NCCL over NVLink on
+GPUs). The per-rank compute of the sequence split is :class:`CudaSequenceShardStep`,
+which drives the ``dcr_shard_*`` entry points of libdcr_b200; there is no CPU path.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+
+from dcr_b200 import _lib
+from dcr_b200.kernel.cuda._common import (HEAD_DIM, cache_strides, check_dtype, check_groups,
+                                          check_k_range, require)
+
+STATE_FLOATS = HEAD_DIM + 2  # (m, l, o[64]) per (b, h) row
+
+
+class TorchComm:
+    """The three collectives of the sharded step over a ``torch.distributed`` group."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self._dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self._gloo = dist.get_backend(group) == "gloo"
+
+    def all_reduce_sum_(self, t: torch.Tensor) -> torch.Tensor:
+        self._dist.all_reduce(t, op=self._dist.ReduceOp.SUM, group=self.group)
+        return t
+
+    def all_gather(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """[world, *t.shape], rank-major."""
+        if out is None:
+            out = torch.empty((self.world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+        if self._gloo:
+            self._dist.all_gather(list(out.unbind(0)), t.contiguous(), group=self.group)
+        else:
+            self._dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
+
+
+def sequence_shard_step(step, comm, bufs: Optional[dict] = None):
+    """One decode step of the sequence split: the per-rank phases of ``step`` with the
+    three collectives between them. Returns O [B, H, D] (identical on every rank).
+
+    ``step`` provides ``score(hist_hi)``, ``refine(hist_hi_sum, hist_lo)``,
+    ``attend(hist_lo_all, world, rank, state)`` and ``combine(states, out)``; ``bufs`` may
+    hold preallocated ``hist_hi``, ``hist_lo``, ``hist_lo_all``, ``state``, ``states`` and
+    ``out``."""
+    bufs = bufs if bufs is not None else {}
+    hist_hi = step.score(bufs.get("hist_hi"))
+    comm.all_reduce_sum_(hist_hi)
+    hist_lo = step.refine(hist_hi, bufs.get("hist_lo"))
+    hist_lo_all = comm.all_gather(hist_lo, bufs.get("hist_lo_all"))
+    state = step.attend(hist_lo_all, comm.world, comm.rank, bufs.get("state"))
+    states = comm.all_gather(state, bufs.get("states"))
+    return step.combine(states, bufs.get("out"))
+
+
+class CudaSequenceShardStep:
+    """This rank's share of a sequence-sharded step on its GPU (libdcr_b200 dcr_shard_*).
+
+    Bind the step's tensors with :meth:`bind`, then the phases run in order; the
+    workspace carries state from one phase to the next."""
+
+    def __init__(self, B: int, H: int, H_kv: int, N_local: int, k_eff: int, *,
+                 dtype: torch.dtype, device: torch.device, eps: float = 1e-12,
+                 workspace_buf: Optional[torch.Tensor] = None):
+        check_groups(H, H_kv)
+        require(N_local > 0, f"N_local must be > 0, got {N_local}")
+        require(k_eff > 0, f"k_eff must be > 0, got {k_eff}")
+        self.B, self.H, self.H_kv, self.N, self.k = B, H, H_kv, N_local, int(k_eff)
+        self.rows = B * H
+        self.cap = min(self.k, N_local)
+        self.dtype = dtype
+        self.dt = _lib.DTYPE_CODES[dtype]
+        self.device = torch.device(device)
+        self.eps = float(eps)
+        self.lib = _lib.load()
+        self.ws_bytes = int(self.lib.dcr_shard_workspace_bytes(B, H, H_kv, N_local, HEAD_DIM,
+                                                               self.k))
+        require(self.ws_bytes > 0, "unsupported shard shape")
+        if workspace_buf is not None:
+            require(workspace_buf.is_cuda and workspace_buf.dtype == torch.uint8 and
+                    workspace_buf.numel() >= self.ws_bytes, "workspace_buf too small")
+            self.ws = workspace_buf
+        else:
+            self.ws = torch.empty(self.ws_bytes, dtype=torch.uint8, device=self.device)
+        self.Q = self.K = self.V = None
+
+    def bind(self, Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> "CudaSequenceShardStep":
+        _lib.require_cuda(Q, K, V)
+        require(Q.shape == (self.B, self.H, HEAD_DIM) and Q.is_contiguous(),
+                f"Q must be a contiguous [{self.B}, {self.H}, {HEAD_DIM}] tensor")
+        want = (self.B, self.H_kv, self.N, HEAD_DIM)
+        require(tuple(K.shape) == want and tuple(V.shape) == want,
+                f"K and V chunks must be {want}, got {tuple(K.shape)}, {tuple(V.shape)}")
+        require(Q.dtype == K.dtype == V.dtype == self.dtype, "Q, K, V must share the dtype")
+        self.ksb, self.ksh = cache_strides(K, "K_chunk")
+        self.vsb, self.vsh = cache_strides(V, "V_chunk")
+        self.Q, self.K, self.V = Q, K, V
+        return self
+
+    def _stream(self) -> int:
+        return _lib.stream_ptr(self.device)
+
+    def _hist(self, out):
+        if out is None:
+            out = torch.empty(self.rows, 256, dtype=torch.int32, device=self.device)
+        return out
+
+    def score(self, hist_hi=None):
+        hist_hi = self._hist(hist_hi)
+        st = self.lib.dcr_shard_score(self.Q.data_ptr(), self.K.data_ptr(), self.dt, self.ksb,
+                                      self.ksh, self.B, self.H, self.H_kv, self.N, HEAD_DIM,
+                                      self.k, self.eps, hist_hi.data_ptr(), self.ws.data_ptr(),
+                                      self.ws_bytes, self._stream())
+        _lib.check(st, "dcr_shard_score")
+        return hist_hi
+
+    def refine(self, hist_hi_sum, hist_lo=None):
+        hist_lo = self._hist(hist_lo)
+        st = self.lib.dcr_shard_refine(self.B, self.H, self.H_kv, self.N, HEAD_DIM, self.k,
+                                       hist_hi_sum.data_ptr(), hist_lo.data_ptr(),
+                                       self.ws.data_ptr(), self.ws_bytes, self._stream())
+        _lib.check(st, "dcr_shard_refine")
+        return hist_lo
+
+    def attend(self, hist_lo_all, world: int, rank: int, state=None):
+        if state is None:
+            state = torch.empty(self.rows, STATE_FLOATS, dtype=torch.float32, device=self.device)
+        st = self.lib.dcr_shard_attend(self.Q.data_ptr(), self.K.data_ptr(), self.V.data_ptr(),
+                                       self.dt, self.ksb, self.ksh, self.vsb, self.vsh, self.B,
+                                       self.H, self.H_kv, self.N, HEAD_DIM, self.k,
+                                       hist_lo_all.data_ptr(), world, rank, state.data_ptr(),
+                                       self.ws.data_ptr(), self.ws_bytes, self._stream())
+        _lib.check(st, "dcr_shard_attend")
+        return state
+
+    def combine(self, states, out=None):
+        world = states.shape[0]
+        if out is None:
+            out = torch.empty(self.B, self.H, HEAD_DIM, dtype=self.dtype, device=self.device)
+        st = self.lib.dcr_shard_combine(states.data_ptr(), world, self.B, self.H, HEAD_DIM,
+                                        self.dt, out.data_ptr(), self._stream())
+        _lib.check(st, "dcr_shard_combine")
+        return out
+
+    def selection(self):
+        """(idx [B, H, min(k, N_local)] int32 local positions ascending, counts [B, H])
+        chosen on this rank by the last :meth:`attend`."""
+        idx = torch.empty(self.B, self.H, self.cap, dtype=torch.int32, device=self.device)
+        cnt = torch.empty(self.B, self.H, dtype=torch.int32, device=self.device)
+        st = self.lib.dcr_shard_selection(self.ws.data_ptr(), self.ws_bytes, self.B, self.H,
+                                          self.H_kv, self.N, HEAD_DIM, self.k, idx.data_ptr(),
+                                          cnt.data_ptr(), self._stream())
+        _lib.check(st, "dcr_shard_selection")
+        return idx, cnt
+
+
+class SequenceShardedDecoder:
+    """Decode steps of one layer whose KV cache is split by sequence across the ranks.
+
+    Construct once per (shape, group): it learns every rank's chunk length with one
+    all-gather, checks ``0 < k_eff < sum(N_r)`` (the reference's caller-side contract,
+    dcr_attention/models/llama/attention.py:806) and allocates the step's buffers. Each
+    call runs :func:`sequence_shard_step` and returns O [B, H, D] on every rank."""
+
+    def __init__(self, B: int, H: int, H_kv: int, N_local: int, k_eff: int, *,
+                 dtype: torch.dtype, device, group=None, comm=None, eps: float = 1e-12):
+        self.device = torch.device(device)
+        self.comm = comm if comm is not None else TorchComm(group)
+        n = torch.tensor([N_local], dtype=torch.int64, device=self.device)
+        self.n_locals = [int(x) for x in self.comm.all_gather(n).view(-1).tolist()]
+        self.offset = sum(self.n_locals[: self.comm.rank])
+        self.n_total = sum(self.n_locals)
+        check_k_range(int(k_eff), self.n_total)
+        self.step = CudaSequenceShardStep(B, H, H_kv, N_local, k_eff, dtype=dtype,
+                                          device=self.device, eps=eps)
+        rows, W = B * H, self.comm.world
+        dev = self.device
+        self.bufs = {
+            "hist_hi": torch.empty(rows, 256, dtype=torch.int32, device=dev),
+            "hist_lo": torch.empty(rows, 256, dtype=torch.int32, device=dev),
+            "hist_lo_all": torch.empty(W, rows, 256, dtype=torch.int32, device=dev),
+            "state": torch.empty(rows, STATE_FLOATS, dtype=torch.float32, device=dev),
+            "states": torch.empty(W, rows, STATE_FLOATS, dtype=torch.float32, device=dev),
+        }
+
+    def __call__(self, Q: torch.Tensor, K_chunk: torch.Tensor, V_chunk: torch.Tensor,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        self.step.bind(Q, K_chunk, V_chunk)
+        if out is not None:
+            require(out.shape == (self.step.B, self.step.H, HEAD_DIM) and out.dtype == Q.dtype
+                    and out.is_contiguous() and out.device == self.device,
+                    "out must be a contiguous [B, H, D] tensor like Q")
+        with torch.cuda.device(self.device):
+            return sequence_shard_step(self.step, self.comm, dict(self.bufs, out=out))
+
+    def selection_global(self):
+        """This rank's selected positions of the last step in global coordinates:
+        (idx [B, H, cap] int64 with offset added, counts [B, H])."""
+        idx, cnt = self.step.selection()
+        return idx.to(torch.int64) + self.offset, cnt
+
+
+def sequence_sharded_attention(Q: torch.Tensor, K_chunk: torch.Tensor, V_chunk: torch.Tensor,
+                               k_eff: int, *, group=None, eps: float = 1e-12) -> torch.Tensor:
+    """One-shot sequence-sharded decode step (see :class:`SequenceShardedDecoder`)."""
+    B, H, _ = Q.shape
+    _, H_kv, N_local, _ = K_chunk.shape
+    dec = SequenceShardedDecoder(B, H, H_kv, N_local, k_eff, dtype=Q.dtype, device=Q.device,
+                                 group=group, eps=eps)
+    return dec(Q, K_chunk, V_chunk)
+
+
+def kv_head_sharded_attention(Q: torch.Tensor, K_heads: torch.Tensor, V_heads: torch.Tensor,
+                              k_eff: int, *, group=None, comm=None, eps: float = 1e-12,
+                              local_attention: Optional[Callable] = None) -> torch.Tensor:
+    """Decode step with the KV heads split across the ranks.
+
+    Q is [B, H, D] (all query heads, the same on every rank); K_heads and V_heads are this
+    rank's KV heads [B, H_kv / W, N, D], rank r owning heads [r*H_kv/W, (r+1)*H_kv/W).
+    Returns O [B, H, D] on every rank. ``local_attention(Q_r, K_r, V_r, k_eff, eps=)``
+    computes the rank's heads (default: the CUDA :func:`topk_qaxis_attention`)."""
+    comm = comm if comm is not None else TorchComm(group)
+    W, r = comm.world, comm.rank
+    require(Q.dim() == 3 and Q.shape[-1] == HEAD_DIM, f"Q must be [B, H, {HEAD_DIM}]")
+    check_dtype(Q, "Q")
+    B, H, D = Q.shape
+    H_kv_local = K_heads.shape[1]
+    H_kv = H_kv_local * W
+    require(H % H_kv == 0, f"H={H} must be divisible by H_kv={H_kv} (= {H_kv_local} x {W})")
+    H_local = H // W
+    if local_attention is None:
+        from dcr_b200.kernel.cuda.topk_axis import topk_qaxis_attention as local_attention
+    Q_r = Q[:, r * H_local:(r + 1) * H_local].contiguous()
+    O_r = local_attention(Q_r, K_heads, V_heads, k_eff, eps=eps)
+    O_all = comm.all_gather(O_r)                 # [W, B, H/W, D]
+    return O_all.permute(1, 0, 2, 3).reshape(B, H, D)

@@ -59,7 +59,10 @@ typedef enum dcr_status {
   DCR_ERR_CUDA = 7,             /* a CUDA runtime call failed                         */
   DCR_ERR_DEVICE_TIMEOUT = 8,   /* device status: a bounded wait expired              */
   DCR_ERR_NOALLOC_LIMIT = 9,    /* shape needs more than DCR_NOALLOC_SCRATCH_BYTES    */
-  DCR_ERR_DEVICE_INDEX = 16     /* device status: an index outside [0, N) was skipped */
+  DCR_ERR_DEVICE_INDEX = 16,    /* device status: an index outside [0, N) was skipped */
+  DCR_ERR_DEVICE_SHARD = 32     /* device status: sharded selection found the global
+                                   histograms inconsistent (fewer than k_eff keys over
+                                   all ranks, or a rank's list overflowed its slots)  */
 } dcr_status;
 
 /* Library ABI version (DCR_ABI_VERSION). */
@@ -152,6 +155,61 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype,
                      int B, int H, int H_kv, int N, int D, int k_eff, float eps,
                      void* O, void* workspace, size_t workspace_bytes, void* stream,
                      void* const* events);
+
+/* ---------------------------------------------------------------------------------
+ * Sequence-sharded decode over several GPUs (exact global top-K).
+ *
+ * No counterpart in the reference: its decode path runs on one GPU. The result is that
+ * of dcr_decode over the whole context: the selected set is the reference's
+ * (_select_topk_indices, dcr_attention/kernel/qaxis_topk_reference.py:91) taken over the
+ * concatenation of the ranks' chunks, and O is _fused_softmax_attention (:148) over it.
+ *
+ * Rank r of `world` holds positions [off_r, off_r + N_local) of every (b, h_kv) cache
+ * row, off_r increasing with r; N_local may differ between ranks. Every rank holds the
+ * whole Q. k_eff is the GLOBAL k (0 < k_eff < sum of N_local). One step is:
+ *   dcr_shard_score   -> caller all-reduces (sum) hist_hi   int32 [B*H][256]
+ *   dcr_shard_refine  -> caller all-gathers  hist_lo  into  int32 [world][B*H][256]
+ *   dcr_shard_attend  -> caller all-gathers  state    into  fp32  [world][B*H][D + 2]
+ *   dcr_shard_combine -> O [B, H, D]
+ * with the same workspace (dcr_shard_workspace_bytes) on all four calls. The workspace
+ * carries state between the calls; do not reuse it for another step in between.
+ * --------------------------------------------------------------------------------- */
+size_t dcr_shard_workspace_bytes(int B, int H, int H_kv, int N_local, int D, int k_eff);
+
+/* Phase 1: Pass 1 over the local chunk and the per-row histogram of the score keys'
+ * high byte (hist_hi, overwritten). */
+int dcr_shard_score(const void* Q, const void* K, int dtype, int64_t k_stride_b,
+                    int64_t k_stride_h, int B, int H, int H_kv, int N_local, int D,
+                    int k_eff, float eps, int32_t* hist_hi, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Phase 2: given hist_hi summed over all ranks, the per-row histogram of the low byte of
+ * the local keys in the threshold's high-byte bin (hist_lo, overwritten). */
+int dcr_shard_refine(int B, int H, int H_kv, int N_local, int D, int k_eff,
+                     const int32_t* hist_hi_sum, int32_t* hist_lo, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* Phase 3: from all ranks' hist_lo (rank-major), this rank's share of the global top-K
+ * (ascending local positions) and the attention over it, written as the unnormalised
+ * fp32 state (m, l, o[D]) of every row (m in base-2 units of the scaled scores; a row
+ * with nothing selected on this rank gets m = -inf, l = 0, o = 0). */
+int dcr_shard_attend(const void* Q, const void* K, const void* V, int dtype,
+                     int64_t k_stride_b, int64_t k_stride_h,
+                     int64_t v_stride_b, int64_t v_stride_h,
+                     int B, int H, int H_kv, int N_local, int D, int k_eff,
+                     const int32_t* hist_lo_all, int world, int rank, float* state,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Phase 4: O [B, H, D] (dtype) from all ranks' states (rank-major). */
+int dcr_shard_combine(const float* states, int world, int B, int H, int D, int dtype, void* O,
+                      void* stream);
+
+/* Copies this rank's selection of the last dcr_shard_attend on `workspace`: idx_out
+ * int32 [B*H][min(k_eff, N_local)] (ascending local positions; row r's first
+ * count_out[r] entries are valid) and count_out int32 [B*H]. Diagnostic. */
+int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, int H, int H_kv,
+                        int N_local, int D, int k_eff, int32_t* idx_out, int32_t* count_out,
+                        void* stream);
 
 /* Synchronises the current device and returns (in *status_out) the OR of the device
  * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.

@@ -1,0 +1,113 @@
+"""Rank bodies of the multi-process sharding tests (spawned processes, one per rank).
+
+``gloo_rank`` runs the host side of both splits on CPU over ``gloo``: the collective
+protocol of dcr_b200.sharded with the CPU restatement (oracle/shard_protocol.py) as each
+rank's compute. ``nccl_rank`` runs the CUDA path over NCCL, one GPU per rank. Each rank
+writes its results to ``out_dir/rank{r}.pt``; the test process checks them.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+
+
+def _paths():
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    for p in (root, os.path.join(root, "dcr-attention_v3_b200"), here):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+
+
+def _bits(t):
+    import numpy as np
+    import torch
+    t = t.contiguous()
+    return t.numpy() if t.dtype == torch.float32 else t.view(torch.int16).numpy().view(np.uint16)
+
+
+def gloo_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    _paths()
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200.sharded import TorchComm, kv_head_sharded_attention, sequence_shard_step
+    from oracle import oracle
+    from oracle.shard_protocol import OracleSequenceShardStep
+    from shard_cases import CASES_BY_WORLD, chunk, make_case
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120))
+    comm = TorchComm()
+    res = {}
+    for name in CASES_BY_WORLD.get(world, []):
+        Q, K, V, splits, k = make_case(name)
+        step = OracleSequenceShardStep(Q, chunk(K, splits, rank), chunk(V, splits, rank), k)
+        O = sequence_shard_step(step, comm)
+        off = sum(splits[:rank])
+        res[name] = {"O": O, "sel": [torch.from_numpy(s + off) for s in step.selection()]}
+
+    # KV-head split: 8 KV heads over the ranks, the rank's heads through the oracle
+    from dcr_b200.synthetic import make_decode_inputs
+    B, H, H_kv, N, k = 2, 32, 8, 700, 106
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=9)
+    hk = H_kv // world
+
+    def local(Qr, Kr, Vr, k_eff, eps=1e-12):
+        O = oracle.decode(_bits(Qr), _bits(Kr), _bits(Vr), "bf16", k_eff, eps)[3]
+        return torch.from_numpy(O)
+
+    if H_kv % world == 0:
+        O_kv = kv_head_sharded_attention(Q, K[:, rank * hk:(rank + 1) * hk].contiguous(),
+                                         V[:, rank * hk:(rank + 1) * hk].contiguous(), k,
+                                         comm=comm, local_attention=local)
+        res["kv_head"] = {"O": O_kv}
+    torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def nccl_cases():
+    """(name, (Q, K, V, splits, k)) of the 2-GPU test, on the CPU."""
+    from shard_cases import make_case
+    return [(n, make_case(n)) for n in ("bf16_2r", "ties_2r", "empty_rank_2r", "gqa2_bf16_2r")]
+
+
+def nccl_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    _paths()
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200.kernel.cuda import topk_qaxis_attention
+    from dcr_b200.sharded import SequenceShardedDecoder, kv_head_sharded_attention
+    from dcr_b200.synthetic import make_decode_inputs
+    from shard_cases import chunk
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = {}
+    for name, (Q, K, V, splits, k) in nccl_cases():
+        B, H, _ = Q.shape
+        dec = SequenceShardedDecoder(B, H, K.shape[1], splits[rank], k, dtype=Q.dtype,
+                                     device=dev)
+        O = dec(Q.to(dev), chunk(K, splits, rank).to(dev), chunk(V, splits, rank).to(dev))
+        idx, cnt = dec.selection_global()
+        idx, cnt = idx.view(B * H, -1).cpu(), cnt.view(-1).cpu()
+        res[name] = {"O": O.cpu(), "sel": [idx[r, :int(cnt[r])].clone() for r in range(B * H)]}
+    B, H, H_kv, N, k = 2, 32, 8, 4096, 614
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=9, device=dev)
+    hk = H_kv // world
+    O = kv_head_sharded_attention(Q, K[:, rank * hk:(rank + 1) * hk], V[:, rank * hk:(rank + 1) * hk],
+                                  k)
+    res["kv_head"] = {"O": O.cpu(), "O_single": topk_qaxis_attention(Q, K, V, k).cpu()}
+    torch.cuda.synchronize()
+    torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
