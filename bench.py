@@ -494,7 +494,8 @@ def run_sharded_arm(args):
     O = torch.empty(B, H, D, dtype=dt, device=dev)
     stream = torch.cuda.current_stream(dev)
     if seq:
-        dec = SequenceShardedDecoder(B, H, H_kv, n_local, k, dtype=dt, device=dev)
+        dec = SequenceShardedDecoder(B, H, H_kv, n_local, k, dtype=dt, device=dev,
+                                     exchange=args.exchange)
 
         def step(i):
             K, V = caches[i % LAYERS]
@@ -525,13 +526,19 @@ def run_sharded_arm(args):
     gpu_index = dev.index
     if os.environ.get("CUDA_VISIBLE_DEVICES"):
         gpu_index = int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[dev.index])
+    # untimed soak of a fixed number of steps that every rank agrees on (each step has
+    # collective phases, so all ranks must run the same count)
+    t0 = time.perf_counter()
+    for i in range(8):
+        step(i)
+    barrier()
+    per_step = (time.perf_counter() - t0) / 8
+    n_soak = torch.tensor([int(args.soak / max(per_step, 1e-6))], dtype=torch.int64, device=dev)
+    dist.all_reduce(n_soak, op=dist.ReduceOp.MAX)
     with ClockSampler(gpu_index) as clk:
-        t_soak = time.perf_counter() + args.soak
-        i = 0
-        while time.perf_counter() < t_soak:
+        for i in range(int(n_soak)):
             step(i)
-            i += 1
-            if i % 32 == 0:
+            if i % 32 == 31:
                 torch.cuda.synchronize(dev)
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -562,7 +569,8 @@ def run_sharded_arm(args):
     clocks = clk.summary()
     status = _lib.read_device_status(clear=True)
 
-    # phase breakdown of the sequence split (events on the launching stream)
+    # phase breakdown of the sequence split with NCCL collectives between the phases
+    # (events on the launching stream; eager launches)
     phases = None
     if seq:
         from dcr_b200.sharded import sequence_shard_step  # noqa: F401  (same phases, timed)
@@ -587,6 +595,33 @@ def run_sharded_arm(args):
         barrier()
         phases = {n: round(statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) * 1e3, 2)
                   for j, n in enumerate(names)}
+
+    # per-kernel times of the peer-exchange step (events between its kernels)
+    peer_kernels = None
+    if seq and args.exchange == "peer":
+        import ctypes
+        names = ["pass1_score", "hist_hi_push", "hist_lo_wait_push", "select_wait",
+                 "pass3_attend_push", "combine_wait"]
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(steps)]
+        for e in evs:
+            for x in e:
+                x.record(stream)
+        st, px = dec.step, dec.peer
+        barrier()
+        for i in range(steps):
+            K, V = caches[i % LAYERS]
+            st.bind(Qs[i % Qs.shape[0]], K, V)
+            arr = (ctypes.c_void_p * 7)(*[x.cuda_event for x in evs[i]])
+            code = st.lib.dcr_shard_decode_peer_timed(
+                st.Q.data_ptr(), st.K.data_ptr(), st.V.data_ptr(), st.dt, st.ksb, st.ksh,
+                st.vsb, st.vsh, st.B, st.H, st.H_kv, st.N, D, st.k, st.eps, px.peers,
+                px.world, px.rank, O.data_ptr(), st.ws.data_ptr(), st.ws_bytes,
+                stream.cuda_stream, arr)
+            if code:
+                raise _lib.DCRError(code, "dcr_shard_decode_peer_timed")
+        barrier()
+        peer_kernels = {n: round(statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) * 1e3,
+                                 2) for j, n in enumerate(names)}
 
     # end to end through the public API: pinned host Q in, O out, host sync per step
     Qh = Qs[:steps].cpu().pin_memory()
@@ -630,16 +665,20 @@ def run_sharded_arm(args):
         "config": {"workload": _workload_name(world, args.split), "B": B, "N": N,
                    "N_per_gpu": n_local, "H": H, "H_kv": H_kv, "H_kv_per_gpu": h_kv_local,
                    "D": D, "k_eff": k, "coverage": CFG["coverage"],
-                   "parallelism": (f"sequence split over {world} GPUs, exact global top-K "
-                                   "(NCCL all-reduce + 2 all-gathers per layer-step)") if seq
-                   else f"KV-head split over {world} GPUs (NCCL all-gather of O)",
+                   "parallelism": (f"sequence split over {world} GPUs, exact global top-K; "
+                                   + ("histogram and state exchange pushed by the kernels "
+                                      "into the peers' buffers over NVLink (no collective)"
+                                      if args.exchange == "peer" else
+                                      "NCCL all-reduce + 2 all-gathers per layer-step"))
+                   if seq else f"KV-head split over {world} GPUs (NCCL all-gather of O)",
                    "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
                          f"{2 * B * h_kv_local * n_local * D * eb / 1e6:.0f} MB per GPU",
                    "launch": "the K timed steps (collectives included) replayed as one CUDA "
                              "graph",
                    "eager_us_per_step": round(ms_eager * 1e3 / steps, 3),
                    "clock_soak_s": args.soak},
-        "phases_us": phases,
+        "nccl_phases_us": phases,
+        "peer_kernels_us": peer_kernels,
         "cpu_baseline": None,
         "e2e": {"value": round(e2e_ms * 1e3 / steps, 3), "unit": UNIT,
                 "h2d_bytes_per_step": B * H * D * eb, "d2h_bytes_per_step": B * H * D * eb,
@@ -652,6 +691,8 @@ def run_sharded_arm(args):
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if seq:
+        dec.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0
@@ -669,6 +710,9 @@ def main():
     ap.add_argument("--split", choices=["seq", "heads"], default="seq",
                     help="multi-GPU layout: context split by sequence (weak scaling, exact "
                          "global top-K) or KV heads split (strong scaling)")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="sequence split: exchange through the kernels' NVLink pushes into "
+                         "the peers' buffers, or NCCL collectives between the phases")
     ap.add_argument("--dtype", choices=["f16", "bf16"], default=CFG["dtype"],
                     help="cache/query dtype (config 1 is fp16)")
     args = ap.parse_args()

@@ -31,6 +31,7 @@
 
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
+#include "dcr_peer.cuh"
 
 namespace dcr {
 
@@ -63,7 +64,33 @@ struct P3Params {
   float* state;             // optional [rows][D + 2]: (m, l, o) instead of O
   float* part;
   int* counters;
+  PeerView pv;              // pv.world > 0 (with state): also copy each row's state into
+                            // slot pv.rank of every peer's exchange buffer (exchange 2)
 };
+
+// Writes a row's (m, l, o) to the state output and, in peer mode, to every peer's slot,
+// then releases the peers' flag. Called by all threads of the CTA; threads 0..D-1 hold o.
+__device__ __forceinline__ void write_state_row(const P3Params& p, int64_t row, float m, float l,
+                                                float o) {
+  const int tid = threadIdx.x;
+  float* st = p.state + row * (kD + 2);
+  if (tid < kD) st[2 + tid] = o;
+  if (tid == 0) {
+    st[0] = m;
+    st[1] = l;
+  }
+  if (p.pv.world <= 0) return;
+  for (int q = 0; q < p.pv.world; ++q) {
+    if (q == p.pv.rank) continue;
+    float* dst = p.pv.st(q, p.pv.rank, row);
+    if (tid < kD) dst[2 + tid] = o;
+    if (tid == 0) {
+      dst[0] = m;
+      dst[1] = l;
+    }
+  }
+  row_pushed(p.pv, 2, p.pv.rows, step_epoch(p.pv));
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kernel(const P3Params p) {
@@ -285,12 +312,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
 
   if (p.S == 1) {
     if (p.state != nullptr) {
-      float* st = p.state + row * (kD + 2);
-      if (tid < kD) st[2 + tid] = od;
-      if (tid == 0) {
-        st[0] = M;
-        st[1] = l_cta;
-      }
+      write_state_row(p, row, M, l_cta, od);
     } else if (tid < kD) {
       ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), od / l_cta);
     }
@@ -309,11 +331,10 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  float Mg = -INFINITY, L = 0.0f, o = 0.0f;
   if (tid < kD) {
     const float* base = p.part + row * p.S * (kD + 2);
-    float Mg = -INFINITY;
     for (int t = 0; t < p.S; ++t) Mg = fmaxf(Mg, __ldcg(base + t * (kD + 2)));
-    float L = 0.0f, o = 0.0f;
     for (int t = 0; t < p.S; ++t) {
       const float* pt = base + t * (kD + 2);
       const float mt = __ldcg(pt);
@@ -321,16 +342,11 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
       L = fmaf(w, __ldcg(pt + 1), L);
       o = fmaf(w, __ldcg(pt + 2 + tid), o);
     }
-    if (p.state != nullptr) {
-      float* st = p.state + row * (kD + 2);
-      st[2 + tid] = o;
-      if (tid == 0) {
-        st[0] = Mg;
-        st[1] = L;
-      }
-    } else {
-      ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), o / L);
-    }
+  }
+  if (p.state != nullptr) {
+    write_state_row(p, row, Mg, L, o);
+  } else if (tid < kD) {
+    ElemTraits<T>::store(p.o, static_cast<int>(row * kD + tid), o / L);
   }
   if (tid == 0) p.counters[row] = 0;
 }
@@ -360,7 +376,7 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
                   int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,
                   const int32_t* idx, const int32_t* counts, int B, int H, int H_kv, int N,
                   int k_eff, void* O, float* state, int splits, float* partials, int* counters,
-                  cudaStream_t st) {
+                  const PeerView* pv, cudaStream_t st) {
   P3Params p;
   p.q = Q;
   p.k = K;
@@ -379,6 +395,8 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
   p.S = splits;
   p.o = O;
   p.state = state;
+  p.pv.world = 0;
+  if (pv != nullptr) p.pv = *pv;
   p.part = partials;
   p.counters = counters;
   switch (dtype) {

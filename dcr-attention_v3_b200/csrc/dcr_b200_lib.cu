@@ -6,4 +6,5 @@
 #include "dcr_attend.cu"
 #include "dcr_shard.cu"
 #include "dcr_capi.cu"
+#include "dcr_peer_capi.cu"
 #include "dcr_noalloc.cu"

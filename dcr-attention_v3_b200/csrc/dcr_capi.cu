@@ -219,7 +219,7 @@ int dcr_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k
   }
   return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx,
                        nullptr, B, H, H_kv, N, k_eff, O, nullptr, w.splits, partials, counters,
-                       s);
+                       nullptr, s);
 }
 
 int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride_b,
@@ -283,7 +283,7 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   if ((st = mark(2))) return st;
   if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx,
                           nullptr, B, H, H_kv, N, k_eff, O, nullptr, w.splits, partials,
-                          counters, s)))
+                          counters, nullptr, s)))
     return st;
   return mark(3);
 }
@@ -341,7 +341,7 @@ int dcr_shard_score(const void* Q, const void* K, int dtype, int64_t k_stride_b,
   if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N_local,
                          reinterpret_cast<uint16_t*>(ws + w.scores), w.n_pad, 1, s)))
     return st;
-  return launch_shard_hist(w, ws, B * H, N_local, k_eff, 0, nullptr, hist_hi, s);
+  return launch_shard_hist(w, ws, B * H, N_local, k_eff, 0, nullptr, hist_hi, nullptr, s);
 }
 
 int dcr_shard_refine(int B, int H, int H_kv, int N_local, int D, int k_eff,
@@ -354,7 +354,7 @@ int dcr_shard_refine(int B, int H, int H_kv, int N_local, int D, int k_eff,
   ShardLayout w;
   if ((st = shard_ws(B, H, N_local, k_eff, workspace, workspace_bytes, w))) return st;
   return launch_shard_hist(w, static_cast<uint8_t*>(workspace), B * H, N_local, k_eff, 1,
-                           hist_hi_sum, hist_lo, static_cast<cudaStream_t>(stream));
+                           hist_hi_sum, hist_lo, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int dcr_shard_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
@@ -375,13 +375,14 @@ int dcr_shard_attend(const void* Q, const void* K, const void* V, int dtype, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rows = B * H;
   // the selection also resets the Pass 3 tickets
-  if ((st = launch_shard_select(w, ws, rows, N_local, k_eff, hist_lo_all, world, rank, s)))
+  if ((st = launch_shard_select(w, ws, rows, N_local, k_eff, hist_lo_all, world, rank, nullptr,
+                                s)))
     return st;
   return launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
                        reinterpret_cast<const int32_t*>(ws + w.idx),
                        reinterpret_cast<const int32_t*>(ws + w.count), B, H, H_kv, N_local,
                        w.cap, nullptr, state, w.splits, reinterpret_cast<float*>(ws + w.partials),
-                       reinterpret_cast<int*>(ws + w.counters), s);
+                       reinterpret_cast<int*>(ws + w.counters), nullptr, s);
 }
 
 int dcr_shard_combine(const float* states, int world, int B, int H, int D, int dtype, void* O,
@@ -391,7 +392,8 @@ int dcr_shard_combine(const float* states, int world, int B, int H, int D, int d
   if (static_cast<int64_t>(B) * H * kD > 0x7fffffffLL) return DCR_ERR_SHAPE;
   if (dtype_bytes(dtype) == 0) return DCR_ERR_DTYPE;
   if (!aligned4(states) || !aligned16(O)) return DCR_ERR_ALIGN;
-  return launch_shard_combine(states, world, B * H, dtype, O, static_cast<cudaStream_t>(stream));
+  return launch_shard_combine(states, world, B * H, dtype, O, nullptr,
+                              static_cast<cudaStream_t>(stream));
 }
 
 int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, int H, int H_kv,

@@ -11,6 +11,8 @@
 
 namespace dcr {
 
+struct PeerView;  // dcr_peer.cuh
+
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 
@@ -69,7 +71,7 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
                   int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h,
                   const int32_t* idx, const int32_t* counts, int B, int H, int H_kv, int N,
                   int k_eff, void* O, float* state, int splits, float* partials, int* counters,
-                  cudaStream_t st);
+                  const struct PeerView* pv, cudaStream_t st);
 
 // Workspace layout of the sequence-sharded step (dcr_shard_*): a dcr_decode layout for
 // the local chunk plus the selection's bookkeeping.
@@ -89,12 +91,16 @@ ShardLayout shard_layout(int rows, int N_local, int k_eff);
 
 // level 0: high-byte histogram of the local keys; level 1: low-byte histogram of the keys
 // in the bin that hist_hi_sum (summed over ranks) puts the k-th largest key in.
+// pv (optional, all launchers below): exchange with the peers' buffers inside the kernels
+// instead of through the caller's collectives.
 int launch_shard_hist(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
-                      int level, const int32_t* hist_hi_sum, int32_t* hist_out, cudaStream_t st);
+                      int level, const int32_t* hist_hi_sum, int32_t* hist_out,
+                      const struct PeerView* pv, cudaStream_t st);
 // This rank's selected positions (ascending) and counts from all ranks' low-byte histograms.
 int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
-                        const int32_t* hist_lo_all, int world, int rank, cudaStream_t st);
+                        const int32_t* hist_lo_all, int world, int rank,
+                        const struct PeerView* pv, cudaStream_t st);
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
-                         cudaStream_t st);
+                         const struct PeerView* pv, cudaStream_t st);
 
 }  // namespace dcr

@@ -34,6 +34,7 @@
 // from the counts of the chunks before it and a block-wide scan inside the chunk.
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
+#include "dcr_peer.cuh"
 
 namespace dcr {
 
@@ -55,6 +56,8 @@ struct ShardParams {
   int32_t* idx;               // [rows][cap] selected local positions, ascending
   int32_t* count;             // [rows] number of selected local positions
   int* counters;              // Pass 3 split-K tickets, reset by phase 3
+  PeerView v;                 // v.world > 0: exchange through the peers' buffers instead of
+                              // hist_hi / hist_out / hist_lo_all
 };
 
 // The 32 keys of this thread in chunk `chunk` of row `row`; 0 past the end of the row
@@ -84,29 +87,48 @@ __device__ __forceinline__ void shard_load_keys(const ShardParams& p, int64_t ro
 
 // Phase 1 (kLevel 0): histogram of key >> 8. Phase 2 (kLevel 1): find BH in the global
 // high-byte histogram, then histogram key & 0xff over the keys in BH.
+// Peer mode: the row's histogram accumulates in this rank's own slot; the last CTA of the
+// row copies it to the peers' buffers and releases their flag (exchange kLevel). Phase 2
+// first waits for the peers' high-byte rows and sums the slots.
 template <int kLevel>
 __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParams p) {
   __shared__ uint32_t h[256];
+  __shared__ uint32_t hsum[256];
   __shared__ uint32_t s_bh;
+  __shared__ int s_last;
   const int tid = threadIdx.x;
   const int64_t row = blockIdx.x / p.chunks;
   const int chunk = blockIdx.x % p.chunks;
+  const bool peer = p.v.world > 0;
+  const uint32_t epoch = peer ? step_epoch(p.v) : 0u;
   h[tid] = 0u;
-  if (kLevel == 1 && tid < 32) {
-    int bin;
-    uint32_t above;
-    warp_find_bin(reinterpret_cast<const uint32_t*>(p.hist_hi + row * 256),
-                  static_cast<uint32_t>(p.k), bin, above);
-    if (tid == 0) {
-      if (bin < 0) {  // fewer than k keys over all ranks
-        raise_status(DCR_ERR_DEVICE_SHARD);
-        bin = 0;
-        above = 0;
-      }
-      s_bh = static_cast<uint32_t>(bin);
-      if (chunk == 0) {
-        p.row_state[row * 4 + 0] = bin;
-        p.row_state[row * 4 + 1] = static_cast<int32_t>(above);
+  if (kLevel == 1) {
+    const uint32_t* hist_hi = reinterpret_cast<const uint32_t*>(p.hist_hi + row * 256);
+    if (peer) {
+      if (tid < 32) wait_peers(p.v, 0, epoch);
+      __syncthreads();
+      uint32_t sum = 0;
+      for (int r = 0; r < p.v.world; ++r)
+        sum += static_cast<uint32_t>(__ldcg(p.v.hh(p.v.rank, r, row) + tid));
+      hsum[tid] = sum;
+      __syncthreads();
+      hist_hi = hsum;
+    }
+    if (tid < 32) {
+      int bin;
+      uint32_t above;
+      warp_find_bin(hist_hi, static_cast<uint32_t>(p.k), bin, above);
+      if (tid == 0) {
+        if (bin < 0) {  // fewer than k keys over all ranks
+          raise_status(DCR_ERR_DEVICE_SHARD);
+          bin = 0;
+          above = 0;
+        }
+        s_bh = static_cast<uint32_t>(bin);
+        if (chunk == 0) {
+          p.row_state[row * 4 + 0] = bin;
+          p.row_state[row * 4 + 1] = static_cast<int32_t>(above);
+        }
       }
     }
   }
@@ -125,7 +147,26 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   }
   __syncthreads();
   const uint32_t c = h[tid];
-  if (c) atomicAdd(reinterpret_cast<unsigned int*>(p.hist_out + row * 256 + tid), c);
+  int32_t* dst = p.hist_out + row * 256;
+  if (peer) dst = kLevel ? p.v.hl(p.v.rank, p.v.rank, row) : p.v.hh(p.v.rank, p.v.rank, row);
+  if (c) atomicAdd(reinterpret_cast<unsigned int*>(dst + tid), c);
+  if (!peer) return;
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = (atomicAdd(p.v.ticket(kLevel, row), 1u) == static_cast<uint32_t>(p.chunks - 1));
+    if (s_last) __threadfence();
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int32_t val = __ldcg(dst + tid);
+  for (int q = 0; q < p.v.world; ++q) {
+    if (q == p.v.rank) continue;
+    int32_t* peer_dst = kLevel ? p.v.hl(q, p.v.rank, row) : p.v.hh(q, p.v.rank, row);
+    peer_dst[tid] = val;
+  }
+  if (tid == 0) *p.v.ticket(kLevel, row) = 0u;
+  row_pushed(p.v, kLevel, p.rows, epoch);
 }
 
 // Phase 3a: T and this rank's tie quota from the gathered low-byte histograms; per-chunk
@@ -141,9 +182,18 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
   const int chunk = blockIdx.x % p.chunks;
   const uint32_t bh = static_cast<uint32_t>(p.row_state[row * 4 + 0]);
   const uint32_t above = static_cast<uint32_t>(p.row_state[row * 4 + 1]);
+  const int32_t* lo_all = p.hist_lo_all;
+  if (p.v.world > 0) {
+    // the peers' low-byte rows land in this rank's hl slots ([world][rows][256] like
+    // hist_lo_all); this rank's own high-byte slot is free again for the next step
+    if (warp == 0) wait_peers(p.v, 1, step_epoch(p.v));
+    if (chunk == 0) p.v.hh(p.v.rank, p.v.rank, row)[tid] = 0;
+    __syncthreads();
+    lo_all = reinterpret_cast<const int32_t*>(p.v.base[p.v.rank] + p.v.lay.hl);
+  }
   uint32_t tot = 0;
   for (int r = 0; r < p.world; ++r)
-    tot += static_cast<uint32_t>(p.hist_lo_all[(static_cast<int64_t>(r) * p.rows + row) * 256 + tid]);
+    tot += static_cast<uint32_t>(__ldcg(lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + tid));
   h[tid] = tot;
   uint32_t key[kShKeys];
   shard_load_keys(p, row, chunk, key);
@@ -162,8 +212,8 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
       const int need = p.k - static_cast<int>(above + above_lo);
       int eq_lower = 0;
       for (int r = 0; r < p.rank; ++r)
-        eq_lower += p.hist_lo_all[(static_cast<int64_t>(r) * p.rows + row) * 256 + bl];
-      const int eq_mine = p.hist_lo_all[(static_cast<int64_t>(p.rank) * p.rows + row) * 256 + bl];
+        eq_lower += __ldcg(lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + bl);
+      const int eq_mine = __ldcg(lo_all + (static_cast<int64_t>(p.rank) * p.rows + row) * 256 + bl);
       const int quota = max(0, min(need - eq_lower, eq_mine));
       s_T = T;
       if (chunk == 0) {
@@ -261,26 +311,44 @@ __global__ void __launch_bounds__(kShThreads) shard_emit_kernel(const ShardParam
     p.count[row] = static_cast<int32_t>(min(s_gt_all + quota, static_cast<uint32_t>(p.cap)));
     p.counters[row] = 0;
   }
+  if (p.v.world > 0 && chunk == 0) p.v.hl(p.v.rank, p.v.rank, row)[tid] = 0;  // read by phase 3a
 }
 
-// Phase 4: merge the ranks' (m, l, o) states of a row into O.
+// Phase 4: merge the ranks' (m, l, o) states of a row into O. Peer mode: wait for the
+// peers' states of the row, read them from this rank's slots, and let the last CTA
+// advance the epoch (the step is complete on this rank).
 template <typename T>
 __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, int world,
-                                                           int rows, void* O) {
+                                                           int rows, void* O, const PeerView v) {
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
+  uint32_t epoch = 0;
+  if (v.world > 0) {
+    epoch = step_epoch(v);
+    if (tid < 32) wait_peers(v, 2, epoch);
+    __syncthreads();
+    states = reinterpret_cast<const float*>(v.base[v.rank] + v.lay.st);
+  }
   float M = -INFINITY;
   for (int r = 0; r < world; ++r)
-    M = fmaxf(M, states[(static_cast<int64_t>(r) * rows + row) * kShStateFloats]);
+    M = fmaxf(M, __ldcg(states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats));
   float L = 0.0f, o = 0.0f;
   for (int r = 0; r < world; ++r) {
     const float* st = states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats;
-    const float m = st[0];
+    const float m = __ldcg(st);
     const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
-    L = fmaf(w, st[1], L);
-    o = fmaf(w, st[2 + tid], o);
+    L = fmaf(w, __ldcg(st + 1), L);
+    o = fmaf(w, __ldcg(st + 2 + tid), o);
   }
   ElemTraits<T>::store(O, static_cast<int>(row * kD + tid), o / L);
+  if (v.world > 0) {
+    __syncthreads();
+    if (tid == 0 && atomicAdd(v.cticket(), 1u) == static_cast<uint32_t>(rows - 1)) {
+      *v.cticket() = 0u;
+      __threadfence();
+      atomicExch(v.epoch(), epoch);
+    }
+  }
 }
 
 size_t align_up_256(size_t x) { return (x + 255) / 256 * 256; }
@@ -313,6 +381,7 @@ ShardLayout shard_layout(int rows, int N_local, int k_eff) {
 static ShardParams shard_params(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
                                 int k_eff) {
   ShardParams p = {};
+  p.v.world = 0;
   p.keys = reinterpret_cast<const uint16_t*>(ws + w.scores);
   p.stride = w.n_pad;
   p.rows = rows;
@@ -331,13 +400,17 @@ static ShardParams shard_params(const ShardLayout& w, uint8_t* ws, int rows, int
 static int check_launch() { return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA; }
 
 int launch_shard_hist(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
-                      int level, const int32_t* hist_hi_sum, int32_t* hist_out, cudaStream_t st) {
+                      int level, const int32_t* hist_hi_sum, int32_t* hist_out,
+                      const PeerView* pv, cudaStream_t st) {
   ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
   p.hist_hi = hist_hi_sum;
   p.hist_out = hist_out;
-  if (cudaMemsetAsync(hist_out, 0, sizeof(int32_t) * 256 * static_cast<size_t>(rows), st) !=
-      cudaSuccess)
+  if (pv != nullptr) {
+    p.v = *pv;
+  } else if (cudaMemsetAsync(hist_out, 0, sizeof(int32_t) * 256 * static_cast<size_t>(rows),
+                             st) != cudaSuccess) {
     return DCR_ERR_CUDA;
+  }
   const int64_t grid = static_cast<int64_t>(rows) * w.chunks;
   if (grid > 0x7fffffff) return DCR_ERR_SHAPE;
   if (level == 0)
@@ -348,9 +421,11 @@ int launch_shard_hist(const ShardLayout& w, uint8_t* ws, int rows, int N_local, 
 }
 
 int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local, int k_eff,
-                        const int32_t* hist_lo_all, int world, int rank, cudaStream_t st) {
+                        const int32_t* hist_lo_all, int world, int rank, const PeerView* pv,
+                        cudaStream_t st) {
   ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
   p.hist_lo_all = hist_lo_all;
+  if (pv != nullptr) p.v = *pv;
   p.world = world;
   p.rank = rank;
   const int64_t grid = static_cast<int64_t>(rows) * w.chunks;
@@ -363,13 +438,19 @@ int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local
 }
 
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
-                         cudaStream_t st) {
+                         const PeerView* pv, cudaStream_t st) {
+  PeerView v = {};
+  if (pv != nullptr) v = *pv;
   switch (dtype) {
     case DCR_DTYPE_BF16:
-      shard_combine_kernel<__nv_bfloat16><<<rows, kD, 0, st>>>(states, world, rows, O);
+      shard_combine_kernel<__nv_bfloat16><<<rows, kD, 0, st>>>(states, world, rows, O, v);
       break;
-    case DCR_DTYPE_F16: shard_combine_kernel<__half><<<rows, kD, 0, st>>>(states, world, rows, O); break;
-    case DCR_DTYPE_F32: shard_combine_kernel<float><<<rows, kD, 0, st>>>(states, world, rows, O); break;
+    case DCR_DTYPE_F16:
+      shard_combine_kernel<__half><<<rows, kD, 0, st>>>(states, world, rows, O, v);
+      break;
+    case DCR_DTYPE_F32:
+      shard_combine_kernel<float><<<rows, kD, 0, st>>>(states, world, rows, O, v);
+      break;
     default: return DCR_ERR_DTYPE;
   }
   return check_launch();

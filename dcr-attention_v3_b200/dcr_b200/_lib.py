@@ -28,6 +28,7 @@ DCR_ERR_DEVICE_TIMEOUT = 8
 DCR_ERR_NOALLOC_LIMIT = 9
 DCR_ERR_DEVICE_INDEX = 16
 DCR_ERR_DEVICE_SHARD = 32
+IPC_HANDLE_BYTES = 64
 
 # Every exported symbol with its (restype, argtypes); tests check this list against the
 # header and the library's dynamic symbol table.
@@ -62,6 +63,19 @@ SIGNATURES = {
     "dcr_shard_combine": (_i32, [_vp, _i32, _i32, _i32, _i32, _i32, _vp, _vp]),
     "dcr_shard_selection": (_i32, [_vp, _sz, _i32, _i32, _i32, _i32, _i32, _i32, _vp, _vp,
                                    _vp]),
+    "dcr_xchg_bytes": (_sz, [_i32, _i32, _i32]),
+    "dcr_xchg_create": (_i32, [_i32, _i32, _i32, ctypes.POINTER(_vp), _vp]),
+    "dcr_xchg_open": (_i32, [_vp, _i32, _i32, _vp, ctypes.POINTER(_vp)]),
+    "dcr_xchg_close": (_i32, [ctypes.POINTER(_vp), _i32, _i32]),
+    "dcr_xchg_destroy": (_i32, [_vp]),
+    "dcr_xchg_reset": (_i32, [_vp, _i32, _i32, _i32, _vp]),
+    "dcr_shard_decode_peer": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32,
+                                     _i32, _i32, _i32, _i32, _f32, ctypes.POINTER(_vp), _i32,
+                                     _i32, _vp, _vp, _sz, _vp]),
+    "dcr_shard_decode_peer_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32,
+                                           _i32, _i32, _i32, _i32, _i32, _f32,
+                                           ctypes.POINTER(_vp), _i32, _i32, _vp, _vp, _sz, _vp,
+                                           ctypes.POINTER(_vp)]),
     "dcr_read_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
 }
 

@@ -21,12 +21,16 @@ dcr_attention/kernel/triton/topk_axis.py:58). Two splits across ranks keep its r
   reference's (_select_topk_indices, qaxis_topk_reference.py:91) over the concatenated
   context; O differs from a single-GPU step only by fp32 summation order.
 
-Collectives go through a :class:`TorchComm` (``torch.distributed``; NCCL over NVLink on
-GPUs). The per-rank compute of the sequence split is :class:`CudaSequenceShardStep`,
-which drives the ``dcr_shard_*`` entry points of libdcr_b200; there is no CPU path.
+The sequence split's exchanges run in one of two ways. ``exchange="peer"`` (default on
+GPUs): the kernels push their histogram and state rows straight into the other ranks'
+exchange buffers over NVLink (CUDA IPC peer memory, :class:`PeerExchange`) and wait on
+per-row flags, so a step is one C call with no host collective (dcr_shard_decode_peer).
+``exchange="nccl"``: the phases of :class:`CudaSequenceShardStep` with three
+``torch.distributed`` collectives (:class:`TorchComm`) between them. There is no CPU path.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 import torch
@@ -53,6 +57,9 @@ class TorchComm:
     def all_reduce_sum_(self, t: torch.Tensor) -> torch.Tensor:
         self._dist.all_reduce(t, op=self._dist.ReduceOp.SUM, group=self.group)
         return t
+
+    def barrier(self) -> None:
+        self._dist.barrier(group=self.group)
 
     def all_gather(self, t: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """[world, *t.shape], rank-major."""
@@ -184,6 +191,53 @@ class CudaSequenceShardStep:
         return idx, cnt
 
 
+class PeerExchange:
+    """This rank's exchange buffer and the mapped buffers of the other ranks (one node).
+
+    Created collectively (every rank of ``comm``, same B and H): each rank allocates and
+    zeroes its buffer (dcr_xchg_create), the IPC handles are all-gathered, and every rank
+    maps the others' (dcr_xchg_open). :meth:`close` unmaps and frees, after a barrier."""
+
+    def __init__(self, B: int, H: int, comm, device):
+        self.lib = _lib.load()
+        self.comm = comm
+        self.world, self.rank = comm.world, comm.rank
+        self.B, self.H = B, H
+        self.device = torch.device(device)
+        require(1 <= self.world <= 8, f"peer exchange connects at most 8 ranks, got {self.world}")
+        self.buf = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.dcr_xchg_create(B, H, self.world, ctypes.byref(self.buf), handle),
+                       "dcr_xchg_create")
+            mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+            allh = comm.all_gather(mine).cpu().numpy().tobytes()
+            self.peers = (ctypes.c_void_p * self.world)()
+            st = self.lib.dcr_xchg_open(allh, self.world, self.rank, self.buf, self.peers)
+        if st:
+            self.lib.dcr_xchg_destroy(self.buf)
+            self.buf = None
+            raise _lib.DCRError(st, "dcr_xchg_open")
+        self._closed = False
+
+    def close(self) -> None:
+        if self._closed or self.buf is None:
+            return
+        self._closed = True
+        torch.cuda.synchronize(self.device)
+        if hasattr(self.comm, "barrier"):
+            self.comm.barrier()
+        with torch.cuda.device(self.device):
+            self.lib.dcr_xchg_close(self.peers, self.world, self.rank)
+            self.lib.dcr_xchg_destroy(self.buf)
+
+    def reset(self) -> None:
+        """Clear the buffer (epoch, flags, abort word); every rank, between steps."""
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.dcr_xchg_reset(self.buf, self.B, self.H, self.world,
+                                               _lib.stream_ptr(self.device)), "dcr_xchg_reset")
+
+
 class SequenceShardedDecoder:
     """Decode steps of one layer whose KV cache is split by sequence across the ranks.
 
@@ -193,9 +247,12 @@ class SequenceShardedDecoder:
     call runs :func:`sequence_shard_step` and returns O [B, H, D] on every rank."""
 
     def __init__(self, B: int, H: int, H_kv: int, N_local: int, k_eff: int, *,
-                 dtype: torch.dtype, device, group=None, comm=None, eps: float = 1e-12):
+                 dtype: torch.dtype, device, group=None, comm=None, eps: float = 1e-12,
+                 exchange: str = "peer"):
+        require(exchange in ("peer", "nccl"), f"exchange must be 'peer' or 'nccl', got {exchange}")
         self.device = torch.device(device)
         self.comm = comm if comm is not None else TorchComm(group)
+        self.exchange = exchange
         n = torch.tensor([N_local], dtype=torch.int64, device=self.device)
         self.n_locals = [int(x) for x in self.comm.all_gather(n).view(-1).tolist()]
         self.offset = sum(self.n_locals[: self.comm.rank])
@@ -212,6 +269,13 @@ class SequenceShardedDecoder:
             "state": torch.empty(rows, STATE_FLOATS, dtype=torch.float32, device=dev),
             "states": torch.empty(W, rows, STATE_FLOATS, dtype=torch.float32, device=dev),
         }
+        self.peer = PeerExchange(B, H, self.comm, dev) if exchange == "peer" else None
+
+    def close(self) -> None:
+        """Release the peer exchange (collective: every rank)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def __call__(self, Q: torch.Tensor, K_chunk: torch.Tensor, V_chunk: torch.Tensor,
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -221,7 +285,18 @@ class SequenceShardedDecoder:
                     and out.is_contiguous() and out.device == self.device,
                     "out must be a contiguous [B, H, D] tensor like Q")
         with torch.cuda.device(self.device):
-            return sequence_shard_step(self.step, self.comm, dict(self.bufs, out=out))
+            if self.peer is None:
+                return sequence_shard_step(self.step, self.comm, dict(self.bufs, out=out))
+            st = self.step
+            if out is None:
+                out = torch.empty(st.B, st.H, HEAD_DIM, dtype=st.dtype, device=self.device)
+            code = st.lib.dcr_shard_decode_peer(
+                st.Q.data_ptr(), st.K.data_ptr(), st.V.data_ptr(), st.dt, st.ksb, st.ksh,
+                st.vsb, st.vsh, st.B, st.H, st.H_kv, st.N, HEAD_DIM, st.k, st.eps,
+                self.peer.peers, self.peer.world, self.peer.rank, out.data_ptr(),
+                st.ws.data_ptr(), st.ws_bytes, st._stream())
+            _lib.check(code, "dcr_shard_decode_peer")
+            return out
 
     def selection_global(self):
         """This rank's selected positions of the last step in global coordinates:
@@ -231,13 +306,18 @@ class SequenceShardedDecoder:
 
 
 def sequence_sharded_attention(Q: torch.Tensor, K_chunk: torch.Tensor, V_chunk: torch.Tensor,
-                               k_eff: int, *, group=None, eps: float = 1e-12) -> torch.Tensor:
-    """One-shot sequence-sharded decode step (see :class:`SequenceShardedDecoder`)."""
+                               k_eff: int, *, group=None, eps: float = 1e-12,
+                               exchange: str = "nccl") -> torch.Tensor:
+    """One-shot sequence-sharded decode step (see :class:`SequenceShardedDecoder`; a
+    decoder kept across steps amortises its setup, which the peer exchange needs)."""
     B, H, _ = Q.shape
     _, H_kv, N_local, _ = K_chunk.shape
     dec = SequenceShardedDecoder(B, H, H_kv, N_local, k_eff, dtype=Q.dtype, device=Q.device,
-                                 group=group, eps=eps)
-    return dec(Q, K_chunk, V_chunk)
+                                 group=group, eps=eps, exchange=exchange)
+    try:
+        return dec(Q, K_chunk, V_chunk)
+    finally:
+        dec.close()
 
 
 def kv_head_sharded_attention(Q: torch.Tensor, K_heads: torch.Tensor, V_heads: torch.Tensor,

@@ -10,7 +10,8 @@
  * Conventions shared by every entry point
  * ---------------------------------------
  *  - All tensor arguments are DEVICE pointers owned by the caller. Inputs are only read.
- *    Outputs are written in place; nothing is allocated by the library.
+ *    Outputs are written in place; nothing is allocated by the library (except the
+ *    exchange buffer of dcr_xchg_create, at setup).
  *  - Shapes follow the reference: Q and O are [B, H, D]; the KV caches are
  *    [B, H_kv, N, D]; scores are [B*H, N]; indices are [B*H, k_eff] int32.
  *    Query head h reads KV head h / (H / H_kv) (GQA).
@@ -41,6 +42,10 @@ extern "C" {
 #define DCR_ABI_VERSION 1
 /* Size of the library-owned scratch array used by dcr_decode_noalloc (16 MiB). */
 #define DCR_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+/* Size of a CUDA IPC handle of an exchange buffer (dcr_xchg_create). */
+#define DCR_IPC_HANDLE_BYTES 64
+/* Most ranks one peer exchange connects. */
+#define DCR_MAX_PEERS 8
 
 typedef enum dcr_dtype {
   DCR_DTYPE_BF16 = 0,
@@ -210,6 +215,51 @@ int dcr_shard_combine(const float* states, int world, int B, int H, int D, int d
 int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, int H, int H_kv,
                         int N_local, int D, int k_eff, int32_t* idx_out, int32_t* count_out,
                         void* stream);
+
+/* ---------------------------------------------------------------------------------
+ * The same sequence-sharded step with the exchanges done inside the kernels, through
+ * the ranks' exchange buffers over NVLink (CUDA IPC peer memory, plain loads and stores,
+ * no multicast), instead of three collectives between phases. No counterpart in the
+ * reference.
+ *
+ * Setup, once per (B, H, world) and rank, all ranks of one node (world <= 8):
+ *   dcr_xchg_create  -> this rank's buffer (cudaMalloc'd, zeroed) and its IPC handle
+ *   (share the handles: all-gather of DCR_IPC_HANDLE_BYTES bytes per rank)
+ *   dcr_xchg_open    -> peers[world]: every rank's buffer mapped into this process
+ * Step (every rank, in the same order, one call each):
+ *   dcr_shard_decode_peer -> O [B, H, D]
+ * Teardown after a barrier: dcr_xchg_close, then dcr_xchg_destroy.
+ * Kernels wait for peers with a bound (2 s): if a peer does not arrive, the wait sets the
+ * device status DCR_ERR_DEVICE_TIMEOUT and the rank's abort word (later waits return at
+ * once), and O of that step is invalid. dcr_xchg_reset (on every rank, between steps,
+ * after a barrier) clears the buffer to start again.
+ * --------------------------------------------------------------------------------- */
+size_t dcr_xchg_bytes(int B, int H, int world);
+int dcr_xchg_create(int B, int H, int world, void** buf_out, void* ipc_handle_out);
+int dcr_xchg_open(const void* ipc_handles, int world, int rank, void* buf, void** peers_out);
+int dcr_xchg_close(void* const* peers, int world, int rank);
+int dcr_xchg_destroy(void* buf);
+int dcr_xchg_reset(void* buf, int B, int H, int world, void* stream);
+
+/* One sequence-sharded decode step of this rank (arguments as dcr_shard_attend, with the
+ * workspace of dcr_shard_workspace_bytes); returns O [B, H, D] on every rank. */
+int dcr_shard_decode_peer(const void* Q, const void* K, const void* V, int dtype,
+                          int64_t k_stride_b, int64_t k_stride_h,
+                          int64_t v_stride_b, int64_t v_stride_h,
+                          int B, int H, int H_kv, int N_local, int D, int k_eff, float eps,
+                          void* const* peers, int world, int rank, void* O,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* dcr_shard_decode_peer with seven caller-created CUDA events recorded on the stream
+ * around its kernels (before Pass 1, after Pass 1, after each histogram, after the
+ * selection, after Pass 3, after the combine). Diagnostic. */
+int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int dtype,
+                                int64_t k_stride_b, int64_t k_stride_h,
+                                int64_t v_stride_b, int64_t v_stride_h,
+                                int B, int H, int H_kv, int N_local, int D, int k_eff,
+                                float eps, void* const* peers, int world, int rank, void* O,
+                                void* workspace, size_t workspace_bytes, void* stream,
+                                void* const* events);
 
 /* Synchronises the current device and returns (in *status_out) the OR of the device
  * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.

@@ -92,15 +92,25 @@ def nccl_rank(rank: int, world: int, port: int, out_dir: str) -> None:
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=120), device_id=dev)
+    from dcr_b200 import _lib
     res = {}
     for name, (Q, K, V, splits, k) in nccl_cases():
         B, H, _ = Q.shape
-        dec = SequenceShardedDecoder(B, H, K.shape[1], splits[rank], k, dtype=Q.dtype,
-                                     device=dev)
-        O = dec(Q.to(dev), chunk(K, splits, rank).to(dev), chunk(V, splits, rank).to(dev))
-        idx, cnt = dec.selection_global()
-        idx, cnt = idx.view(B * H, -1).cpu(), cnt.view(-1).cpu()
-        res[name] = {"O": O.cpu(), "sel": [idx[r, :int(cnt[r])].clone() for r in range(B * H)]}
+        Kc, Vc = chunk(K, splits, rank).to(dev), chunk(V, splits, rank).to(dev)
+        r = {}
+        for ex in ("nccl", "peer"):
+            dec = SequenceShardedDecoder(B, H, K.shape[1], splits[rank], k, dtype=Q.dtype,
+                                         device=dev, exchange=ex)
+            for _ in range(3):   # repeated steps: the peer exchange's epochs advance
+                O = dec(Q.to(dev), Kc, Vc)
+            idx, cnt = dec.selection_global()
+            idx, cnt = idx.view(B * H, -1).cpu(), cnt.view(-1).cpu()
+            sfx = "" if ex == "nccl" else "_peer"
+            r["O" + sfx] = O.cpu()
+            r["sel" + sfx] = [idx[i, :int(cnt[i])].clone() for i in range(B * H)]
+            dec.close()
+        r["status"] = _lib.read_device_status(clear=True)
+        res[name] = r
     B, H, H_kv, N, k = 2, 32, 8, 4096, 614
     Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=9, device=dev)
     hk = H_kv // world

@@ -159,6 +159,59 @@ def test_decoder_rejects_k_not_below_total(cuda_lib):
                                comm=OneRank())
 
 
+class _OneRank:
+    world, rank = 1, 0
+
+    def all_gather(self, t, out=None):
+        return t.unsqueeze(0)
+
+    def barrier(self):
+        pass
+
+
+def test_peer_exchange_single_rank_steps(oracle_mod, cuda_lib):
+    """The peer-exchange step with one rank: every kernel of the fused path (no peer to
+    wait for), over consecutive steps (the epoch advances), eager and as a graph replay."""
+    from dcr_b200 import _lib
+    from dcr_b200.sharded import SequenceShardedDecoder
+    from dcr_b200.synthetic import fresh_queries, make_decode_inputs
+    B, H, H_kv, N, k = 2, 32, 8, 5000, 750
+    _, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=4)
+    Qs = fresh_queries(4, B, H, dtype=torch.bfloat16, seed=6)
+    Kd, Vd = K.to(DEV), V.to(DEV)
+    dec = SequenceShardedDecoder(B, H, H_kv, N, k, dtype=torch.bfloat16, device=DEV,
+                                 comm=_OneRank(), exchange="peer")
+    outs = []
+    for i in range(3):
+        Q = Qs[i].contiguous()
+        O = dec(Q.to(DEV), Kd, Vd)
+        idx, cnt = dec.selection_global()
+        assert _lib.read_device_status(clear=True) == 0
+        _, _, ref_idx, O_ref = oracle_mod.decode(to_np(Q), to_np(K), to_np(V), "bf16", k)
+        assert bool((cnt == k).all())
+        assert np.array_equal(idx.view(B * H, k).cpu().numpy(), ref_idx.astype(np.int64))
+        ok, st = attention_close(O.float().cpu().numpy(), O_ref, got_rounded_to="bf16")
+        assert ok, (i, st)
+        outs.append(O.clone())
+    # the same three steps captured once and replayed
+    Qd = torch.empty(B, H, 64, dtype=torch.bfloat16, device=DEV)
+    Od = torch.empty_like(Qd)
+    g = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(DEV)
+    side.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(g, stream=side):
+            dec(Qd, Kd, Vd, out=Od)
+        for i in range(3):
+            Qd.copy_(Qs[i].to(DEV))
+            g.replay()
+            side.synchronize()
+            assert torch.equal(Od, outs[i]), i
+    assert _lib.read_device_status(clear=True) == 0
+    del g
+    dec.close()
+
+
 # ---- two GPUs: the real NCCL path ------------------------------------------------------
 def _free_port() -> int:
     with socket.socket() as s:
@@ -196,6 +249,12 @@ def test_two_gpus_nccl(oracle_mod, tmp_path):
         assert ok, (name, st)
     # KV-head split: same O on both ranks; against the single-GPU step only the split-K
     # summation order differs (its split factor follows the rank's row count)
+    for name, _ in shard_workers.nccl_cases():
+        for w in range(2):     # peer-memory exchange: same selection and O as over NCCL
+            assert torch.equal(res[w][name]["O_peer"], res[w][name]["O"]), (name, w)
+            for a, b in zip(res[w][name]["sel_peer"], res[w][name]["sel"]):
+                assert torch.equal(a, b), (name, w)
+            assert res[w][name]["status"] == 0
     kv = res[0]["kv_head"]
     assert torch.equal(res[1]["kv_head"]["O"], kv["O"])
     ok, st = attention_close(kv["O"].float().numpy(), kv["O_single"].float().numpy(),
