@@ -371,6 +371,67 @@ def run_gpu_arm(args):
     dom = kern[dom_name]
     traffic = _read_profile_traffic(dom_name)
 
+    # ---- projected-score mode (rank-16 keys written at append) on the same layers --------
+    from dcr_b200.kernel.cuda import project_keys
+    from dcr_b200.synthetic import projection_matrix
+    Pd = projection_matrix(seed=0, device=dev)
+    kps = [project_keys(K, Pd) for K, _ in caches]
+    kpsb, kpsh = kps[0].stride(0), kps[0].stride(1)
+    sc_buf = torch.empty(B * H, N, dtype=torch.int16, device=dev)
+
+    def step_proj(i, sptr):
+        K, V = caches[i % LAYERS]
+        st = lib.dcr_decode_projected(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), V.data_ptr(),
+                                      kps[i % LAYERS].data_ptr(), dcode, ksb, ksh, ksb, ksh,
+                                      kpsb, kpsh, Pd.data_ptr(), 16, B, H, H_kv, N, D, k, 1e-12,
+                                      O.data_ptr(), ws.data_ptr(), ws_n, sptr)
+        if st:
+            raise _lib.DCRError(st, "dcr_decode_projected")
+
+    def pass1_proj(i, sptr):
+        st = lib.dcr_score_projected(kps[i % LAYERS].data_ptr(), dcode, kpsb, kpsh,
+                                     Qs[i % Qs.shape[0]].data_ptr(), 1e-12, Pd.data_ptr(), 16, B,
+                                     H, H_kv, N, D, sc_buf.data_ptr(), N, sptr)
+        if st:
+            raise _lib.DCRError(st, "dcr_score_projected")
+
+    def graph_ms(fn):
+        """Device time of `steps` calls of fn replayed as one CUDA graph (after a warm replay)."""
+        for i in range(3):
+            fn(i, sp)
+        barrier()
+        cap2 = torch.cuda.Stream(dev)
+        cap2.wait_stream(stream)
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=cap2):
+            for i in range(steps):
+                fn(i, cap2.cuda_stream)
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cap2):
+            g2.replay()
+            barrier()
+            a.record(cap2)
+            g2.replay()
+            z.record(cap2)
+        barrier()
+        del g2
+        return a.elapsed_time(z)
+
+    proj_us = graph_ms(step_proj) * 1e3 / steps
+    p1p_us = graph_ms(pass1_proj) * 1e3 / steps
+    bytes_p1p = B * H_kv * N * 16 * eb + B * H * N * 2 + B * H * D * eb
+    projected = {
+        "us_per_layer": round(proj_us, 3),
+        "pass1_us": round(p1p_us, 2), "pass1_bytes": bytes_p1p,
+        "pass1_gbs": round(bytes_p1p / p1p_us / 1e3, 1),
+        "pass1_frac_of_hbm": round(bytes_p1p / p1p_us / 1e3 / _peaks()[0], 3),
+        "what": "same layers with KP = K.P (P: seeded 64x16 Gaussian, rank 16) written by "
+                "dcr_project_keys; Pass 1 reads 32-byte KP rows; selection bit-exact vs the "
+                "CPU restatement (no reference counterpart)",
+    }
+    status |= _lib.read_device_status(clear=True)
+
     # ---- end to end through the public API with host buffers ---------------------------
     Qh = Qs[:steps].cpu().pin_memory()
     Oh = torch.empty(steps, B, H, D, dtype=dt).pin_memory()
@@ -430,6 +491,7 @@ def run_gpu_arm(args):
                      "frac": round(dom["gbs"] / peak, 3),
                      "traffic": traffic, "algorithmic_bytes": dom["bytes"]},
         "kernels": kern,
+        "projected_r16": projected,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_ms * 1e3 / (steps * world), 3), "unit": UNIT,
                 "h2d_bytes_per_step": B * H * D * eb, "d2h_bytes_per_step": B * H * D * eb,

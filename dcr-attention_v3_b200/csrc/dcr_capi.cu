@@ -245,11 +245,35 @@ int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride
   return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
 }
 
+// Projected-score inputs of a decode step (null kp: the exact Pass 1 on K).
+struct ProjArgs {
+  const void* kp;
+  int64_t psb, psh;
+  const float* P;
+};
+
+static int check_proj(const void* KP, int dtype, int64_t& psb, int64_t& psh, int B, int H_kv,
+                      int N, const float* P, int R) {
+  if (KP == nullptr || P == nullptr) return DCR_ERR_NULL;
+  if (R != DCR_PROJ_RANK) return DCR_ERR_SHAPE;
+  const size_t eb = dtype_bytes(dtype);
+  if (eb == 0) return DCR_ERR_DTYPE;
+  if (H_kv == 1) psh = static_cast<int64_t>(N) * R;
+  if (B == 1) psb = psh * H_kv;
+  if (!aligned16(KP) || (reinterpret_cast<uintptr_t>(P) & 3u) != 0) return DCR_ERR_ALIGN;
+  if (psb < 0 || psh < 0) return DCR_ERR_SHAPE;
+  if ((psb * static_cast<int64_t>(eb)) % 16 != 0 || (psh * static_cast<int64_t>(eb)) % 16 != 0)
+    return DCR_ERR_ALIGN;
+  if (H_kv > 1 && psh < static_cast<int64_t>(N) * R) return DCR_ERR_SHAPE;
+  if (B > 1 && psb < static_cast<int64_t>(N) * R) return DCR_ERR_SHAPE;
+  return DCR_OK;
+}
+
 static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
                        int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                        int64_t v_stride_h, int B, int H, int H_kv, int N, int D, int k_eff,
                        float eps, void* O, void* workspace, size_t workspace_bytes,
-                       void* stream, void* const* events) {
+                       void* stream, void* const* events, const ProjArgs* proj = nullptr) {
   int st = check_heads(B, H, H_kv, N, D);
   if (st) return st;
   if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
@@ -274,9 +298,13 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   };
   if ((st = mark(0))) return st;
   // Pass 1 stores order keys, which Pass 2 reads directly.
-  if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
-                         w.n_pad, 1, s)))
-    return st;
+  if (proj != nullptr)
+    st = launch_score_projected(proj->kp, dtype, proj->psb, proj->psh, Q, proj->P, eps, B, H,
+                                H_kv, N, scores, w.n_pad, 1, s);
+  else
+    st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
+                      w.n_pad, 1, s);
+  if (st) return st;
   if ((st = mark(1))) return st;
   // Pass 2 also resets the Pass 3 split-K tickets of its row.
   if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s))) return st;
@@ -305,6 +333,89 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype, int
     if (events[i] == nullptr) return DCR_ERR_NULL;
   return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
                      N, D, k_eff, eps, O, workspace, workspace_bytes, stream, events);
+}
+
+// ---- projected-score mode --------------------------------------------------------------
+
+int dcr_project_keys(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h, int B,
+                     int H_kv, int N, int D, const float* P, int R, void* KP,
+                     int64_t p_stride_b, int64_t p_stride_h, void* stream) {
+  if (B <= 0 || H_kv <= 0 || N <= 0 || D != kD) return DCR_ERR_SHAPE;
+  int st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N);
+  if (st) return st;
+  if ((st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R))) return st;
+  return launch_append(K, K, k_stride_b, k_stride_h, nullptr, nullptr, 0, 0, KP, p_stride_b,
+                       p_stride_h, P, B, H_kv, N, 0, dtype, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_cache_append(const void* K_new, const void* V_new, int dtype, int64_t new_stride_b,
+                     int64_t new_stride_h, int B, int H_kv, int n_new, int D, void* K_cache,
+                     void* V_cache, int64_t c_stride_b, int64_t c_stride_h, int pos, int N_max,
+                     const float* P, int R, void* KP_cache, int64_t p_stride_b,
+                     int64_t p_stride_h, void* stream) {
+  if (B <= 0 || H_kv <= 0 || n_new <= 0 || N_max <= 0 || D != kD) return DCR_ERR_SHAPE;
+  if (pos < 0 || static_cast<int64_t>(pos) + n_new > N_max) return DCR_ERR_SHAPE;
+  int64_t vsb = new_stride_b, vsh = new_stride_h, cvb = c_stride_b, cvh = c_stride_h;
+  int st = check_cache(K_new, dtype, new_stride_b, new_stride_h, B, H_kv, n_new);
+  if (st) return st;
+  if ((st = check_cache(V_new, dtype, vsb, vsh, B, H_kv, n_new))) return st;
+  if ((st = check_cache(K_cache, dtype, c_stride_b, c_stride_h, B, H_kv, N_max))) return st;
+  if ((st = check_cache(V_cache, dtype, cvb, cvh, B, H_kv, N_max))) return st;
+  if (KP_cache != nullptr || P != nullptr)
+    if ((st = check_proj(KP_cache, dtype, p_stride_b, p_stride_h, B, H_kv, N_max, P, R)))
+      return st;
+  return launch_append(K_new, V_new, new_stride_b, new_stride_h, K_cache, V_cache, c_stride_b,
+                       c_stride_h, KP_cache, p_stride_b, p_stride_h, P, B, H_kv, n_new, pos,
+                       dtype, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
+                        const void* Q, float eps, const float* P, int R, int B, int H, int H_kv,
+                        int N, int D, uint16_t* scores, int64_t s_stride_row, void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  if ((st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R))) return st;
+  if (Q == nullptr || scores == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q)) return DCR_ERR_ALIGN;
+  if (s_stride_row < N) return DCR_ERR_SHAPE;
+  return launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, eps, B, H, H_kv, N,
+                                scores, s_stride_row, 0, static_cast<cudaStream_t>(stream));
+}
+
+int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64_t p_stride_b,
+                                 int64_t p_stride_h, const float* P, int R, int B, int H,
+                                 int H_kv, int N, int D, int k_eff, float eps, int32_t* idx_out,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  int st = check_heads(B, H, H_kv, N, D);
+  if (st) return st;
+  if ((st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R))) return st;
+  if (Q == nullptr || idx_out == nullptr) return DCR_ERR_NULL;
+  if (!aligned16(Q)) return DCR_ERR_ALIGN;
+  if ((st = check_k(k_eff, N))) return st;
+  const int rows = B * H;
+  const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
+  if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
+  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
+  uint16_t* scores = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + w.scores);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((st = launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, eps, B, H, H_kv, N,
+                                   scores, w.n_pad, 1, s)))
+    return st;
+  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
+}
+
+int dcr_decode_projected(const void* Q, const void* K, const void* V, const void* KP, int dtype,
+                         int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                         int64_t v_stride_h, int64_t p_stride_b, int64_t p_stride_h,
+                         const float* P, int R, int B, int H, int H_kv, int N, int D, int k_eff,
+                         float eps, void* O, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (B <= 0 || H_kv <= 0 || N <= 0) return DCR_ERR_SHAPE;
+  const int st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R);
+  if (st) return st;
+  const ProjArgs proj = {KP, p_stride_b, p_stride_h, P};
+  return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
+                     N, D, k_eff, eps, O, workspace, workspace_bytes, stream, nullptr, &proj);
 }
 
 // ---- sequence-sharded decode ----------------------------------------------------------

@@ -103,4 +103,16 @@ int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
                          const struct PeerView* pv, cudaStream_t st);
 
+// Projected-score mode (dcr_project.cu). Append: copies n_new rows of K and V into the
+// caches at position pos (k_cache may be null: no copy) and writes their projection
+// KP = K . P (kp may be null). Score: Pass 1 from KP [B, H_kv, N, R] and P [D][R].
+int launch_append(const void* k_new, const void* v_new, int64_t nsb, int64_t nsh, void* k_cache,
+                  void* v_cache, int64_t csb, int64_t csh, void* kp, int64_t psb, int64_t psh,
+                  const float* P, int B, int H_kv, int n_new, int pos, int dtype,
+                  cudaStream_t st);
+int launch_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
+                           const void* Q, const float* P, float eps, int B, int H, int H_kv,
+                           int N, uint16_t* scores, int64_t s_stride, int keys_out,
+                           cudaStream_t st);
+
 }  // namespace dcr

@@ -29,6 +29,7 @@ DCR_ERR_NOALLOC_LIMIT = 9
 DCR_ERR_DEVICE_INDEX = 16
 DCR_ERR_DEVICE_SHARD = 32
 IPC_HANDLE_BYTES = 64
+PROJ_RANK = 16
 
 # Every exported symbol with its (restype, argtypes); tests check this list against the
 # header and the library's dynamic symbol table.
@@ -54,6 +55,17 @@ SIGNATURES = {
     "dcr_decode_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                                 _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp,
                                 ctypes.POINTER(_vp)]),
+    "dcr_project_keys": (_i32, [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
+                                _i64, _i64, _vp]),
+    "dcr_cache_append": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp,
+                                _i64, _i64, _i32, _i32, _vp, _i32, _vp, _i64, _i64, _vp]),
+    "dcr_score_projected": (_i32, [_vp, _i32, _i64, _i64, _vp, _f32, _vp, _i32, _i32, _i32,
+                                   _i32, _i32, _i32, _vp, _i64, _vp]),
+    "dcr_select_indices_projected": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i32, _i32,
+                                            _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "dcr_decode_projected": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
+                                    _vp, _vp, _sz, _vp]),
     "dcr_shard_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "dcr_shard_score": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,
                                _f32, _vp, _vp, _sz, _vp]),

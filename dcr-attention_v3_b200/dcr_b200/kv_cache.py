@@ -1,0 +1,82 @@
+"""Preallocated decode KV cache written in place (optionally with projected keys).
+
+The reference's Llama hook keeps K and V in HF ``DynamicCache`` (dcr_attention/models/
+llama/compat.py:208-254; attention.py:422), whose ``update`` concatenates the whole cache
+with the new token every step (an O(N) copy), and then repeats or strides the KV heads
+for the kernel (attention.py:425-426, :810-811). :class:`StaticKVCache` allocates
+``[B, H_kv, N_max, D]`` K and V once and appends new tokens in place with one kernel
+(dcr_cache_append), which also writes the rank-16 projected keys ``KP = K . P`` used by
+the projected-score mode. The views it hands out (``K``, ``V``, ``KP``: the first
+``length`` positions) are strided views that every kernel of this package accepts
+without a copy.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from dcr_b200 import _lib
+from dcr_b200.kernel.cuda._common import HEAD_DIM, cache_strides, check_dtype, require
+from dcr_b200.kernel.cuda.projected import PROJ_RANK, check_projection, kp_strides
+
+
+class StaticKVCache:
+    """One layer's K/V (and projected-key) cache for ``B`` sequences of up to ``N_max``
+    positions, filled from position 0 by :meth:`append`."""
+
+    def __init__(self, B: int, H_kv: int, N_max: int, *, dtype: torch.dtype, device,
+                 P: Optional[torch.Tensor] = None):
+        self.device = torch.device(device)
+        check_dtype(torch.empty(0, dtype=dtype), "cache")
+        self.B, self.H_kv, self.N_max, self.dtype = B, H_kv, N_max, dtype
+        shape = (B, H_kv, N_max, HEAD_DIM)
+        self.k = torch.empty(shape, dtype=dtype, device=self.device)
+        self.v = torch.empty(shape, dtype=dtype, device=self.device)
+        self.P = check_projection(P, self.device) if P is not None else None
+        self.kp = (torch.empty(B, H_kv, N_max, PROJ_RANK, dtype=dtype, device=self.device)
+                   if P is not None else None)
+        self.length = 0
+
+    @property
+    def K(self) -> torch.Tensor:
+        return self.k[:, :, :self.length]
+
+    @property
+    def V(self) -> torch.Tensor:
+        return self.v[:, :, :self.length]
+
+    @property
+    def KP(self) -> Optional[torch.Tensor]:
+        return None if self.kp is None else self.kp[:, :, :self.length]
+
+    def append(self, K_new: torch.Tensor, V_new: torch.Tensor) -> None:
+        """Writes ``[B, H_kv, n_new, D]`` new keys and values (and their projections) at
+        positions ``[length, length + n_new)``; stream-ordered, no synchronisation."""
+        _lib.require_cuda(K_new, V_new)
+        require(tuple(K_new.shape) == tuple(V_new.shape) and K_new.dim() == 4 and
+                K_new.shape[0] == self.B and K_new.shape[1] == self.H_kv,
+                f"K_new and V_new must be [{self.B}, {self.H_kv}, n_new, {HEAD_DIM}]")
+        require(K_new.dtype == self.dtype and V_new.dtype == self.dtype,
+                f"new rows must be {self.dtype}")
+        n_new = K_new.shape[2]
+        require(self.length + n_new <= self.N_max,
+                f"cache full: {self.length} + {n_new} > N_max={self.N_max}")
+        nsb, nsh = cache_strides(K_new, "K_new")
+        require(cache_strides(V_new, "V_new") == (nsb, nsh) or n_new == 1 or
+                V_new.stride() == K_new.stride(), "K_new and V_new must share strides")
+        csb, csh = cache_strides(self.k, "K_cache")
+        if self.kp is not None:
+            psb, psh = kp_strides(self.kp)
+            P_ptr, kp_ptr = self.P.data_ptr(), self.kp.data_ptr()
+        else:
+            psb = psh = 0
+            P_ptr = kp_ptr = None
+        with torch.cuda.device(self.device):
+            st = _lib.load().dcr_cache_append(
+                K_new.data_ptr(), V_new.data_ptr(), _lib.DTYPE_CODES[self.dtype], nsb, nsh,
+                self.B, self.H_kv, n_new, HEAD_DIM, self.k.data_ptr(), self.v.data_ptr(), csb,
+                csh, self.length, self.N_max, P_ptr, PROJ_RANK, kp_ptr, psb, psh,
+                _lib.stream_ptr(self.device))
+        _lib.check(st, "dcr_cache_append")
+        self.length += n_new

@@ -42,6 +42,8 @@ extern "C" {
 #define DCR_ABI_VERSION 1
 /* Size of the library-owned scratch array used by dcr_decode_noalloc (16 MiB). */
 #define DCR_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+/* Rank of the key projection of the projected-score mode (dcr_*_projected). */
+#define DCR_PROJ_RANK 16
 /* Size of a CUDA IPC handle of an exchange buffer (dcr_xchg_create). */
 #define DCR_IPC_HANDLE_BYTES 64
 /* Most ranks one peer exchange connects. */
@@ -160,6 +162,53 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype,
                      int B, int H, int H_kv, int N, int D, int k_eff, float eps,
                      void* O, void* workspace, size_t workspace_bytes, void* stream,
                      void* const* events);
+
+/* ---------------------------------------------------------------------------------
+ * Projected-score mode. No counterpart in the reference (its Pass 1 always reads the
+ * 64-dim keys): the cache also holds KP = K . P, the keys projected by a fixed
+ * DCR_HEAD_DIM x DCR_PROJ_RANK fp32 matrix P (row-major, P[d * R + j]), stored in the
+ * cache dtype as [B, H_kv, N, R] with contiguous rows of R elements. Pass 1 then scores
+ * bf16(KP . (u . P)), reading R instead of D elements per key; Pass 2 and Pass 3 are
+ * those of dcr_decode. The reference's DynamicCache.update (dcr_attention/models/llama/
+ * compat.py:208-254), a torch.cat of the whole cache per step, becomes dcr_cache_append
+ * into preallocated caches. R must be DCR_PROJ_RANK; P must be 4-byte aligned.
+ * --------------------------------------------------------------------------------- */
+
+/* KP [B, H_kv, N, R] of the N rows of an existing K cache (prefill). */
+int dcr_project_keys(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
+                     int B, int H_kv, int N, int D, const float* P, int R, void* KP,
+                     int64_t p_stride_b, int64_t p_stride_h, void* stream);
+
+/* Writes n_new rows of K_new and V_new ([B, H_kv, n_new, D], one pair of strides for
+ * both) into K_cache and V_cache ([B, H_kv, N_max, D], one pair of strides) at positions
+ * [pos, pos + n_new), and, if KP_cache and P are given, their projections into KP_cache
+ * at the same positions. pos + n_new must not exceed N_max. */
+int dcr_cache_append(const void* K_new, const void* V_new, int dtype,
+                     int64_t new_stride_b, int64_t new_stride_h, int B, int H_kv, int n_new,
+                     int D, void* K_cache, void* V_cache, int64_t c_stride_b,
+                     int64_t c_stride_h, int pos, int N_max, const float* P, int R,
+                     void* KP_cache, int64_t p_stride_b, int64_t p_stride_h, void* stream);
+
+/* Pass 1 of the projected mode: bf16 score bits [B*H, N] (row stride s_stride_row). */
+int dcr_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
+                        const void* Q, float eps, const float* P, int R, int B, int H,
+                        int H_kv, int N, int D, uint16_t* scores, int64_t s_stride_row,
+                        void* stream);
+
+/* Pass 1 (projected) + Pass 2: indices [B*H, k_eff] int32 ascending. Workspace as
+ * dcr_workspace_bytes. */
+int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64_t p_stride_b,
+                                 int64_t p_stride_h, const float* P, int R, int B, int H,
+                                 int H_kv, int N, int D, int k_eff, float eps, int32_t* idx_out,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Full decode step with projected Pass 1: O [B, H, D]. Workspace as dcr_workspace_bytes. */
+int dcr_decode_projected(const void* Q, const void* K, const void* V, const void* KP, int dtype,
+                         int64_t k_stride_b, int64_t k_stride_h,
+                         int64_t v_stride_b, int64_t v_stride_h,
+                         int64_t p_stride_b, int64_t p_stride_h, const float* P, int R,
+                         int B, int H, int H_kv, int N, int D, int k_eff, float eps, void* O,
+                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Sequence-sharded decode over several GPUs (exact global top-K).

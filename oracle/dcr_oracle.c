@@ -16,6 +16,16 @@
  *   oracle_attend       _gather_kv + _fused_softmax_attention
  *                                                   qaxis_topk_reference.py:111-193
  *
+ * Projected-score mode (no counterpart in the reference; the rank-R projection P of the
+ * keys is written at cache-append time and the unit query is projected with the same P):
+ *
+ *   oracle_project_keys      KP = round_dtype(K . P), fmaf chain over d = 0..63
+ *   oracle_query_projection  qp = u . P (fp32), fmaf chain over d = 0..63
+ *   oracle_scores_projected  bf16_rne(even + odd): two fmaf chains of KP . qp, one over
+ *                            the even j, one over the odd j, added at the end
+ *
+ * Their parity is pinned against this restatement only (the reference has no such mode).
+ *
  * Pinning: tests/test_oracle_golden.py checks these functions against golden vectors the
  * reference itself produced (tests/golden/make_golden.py).
  *
@@ -83,6 +93,37 @@ static inline uint16_t f32_to_bf16_rne(float f) {
   return (uint16_t)(b >> 16);
 }
 
+/* fp32 -> fp16, IEEE round-to-nearest-even (overflow to inf, subnormals, quiet NaN). */
+static inline uint16_t f32_to_f16_rne(float f) {
+  const uint32_t x = f32_to_bits(f);
+  const uint32_t sign = (x >> 16) & 0x8000u;
+  const uint32_t ax = x & 0x7fffffffu;
+  if (ax > 0x7f800000u) return (uint16_t)(sign | 0x7e00u);
+  if (ax >= 0x477ff000u) return (uint16_t)(sign | 0x7c00u); /* >= 65520 rounds to inf */
+  if (ax < 0x38800000u) {                                   /* below 2^-14: subnormal   */
+    if (ax <= 0x33000000u) return (uint16_t)sign;           /* <= 2^-25 rounds to zero  */
+    const uint32_t e = ax >> 23;
+    const uint32_t m = (ax & 0x7fffffu) | 0x800000u;
+    const uint32_t shift = 126u - e; /* value = m * 2^(e-150); units of 2^-24 */
+    uint32_t q = m >> shift;
+    const uint32_t rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1u);
+    if (rem > half || (rem == half && (q & 1u))) ++q;
+    return (uint16_t)(sign | q);
+  }
+  uint32_t q = (((ax >> 23) - 112u) << 10) | ((ax & 0x7fffffu) >> 13);
+  const uint32_t rem = ax & 0x1fffu;
+  if (rem > 0x1000u || (rem == 0x1000u && (q & 1u))) ++q;
+  return (uint16_t)(sign | q);
+}
+
+static inline void store_elem(void* base, int dtype, int64_t i, float v) {
+  switch (dtype) {
+    case ORACLE_BF16: ((uint16_t*)base)[i] = f32_to_bf16_rne(v); break;
+    case ORACLE_F16: ((uint16_t*)base)[i] = f32_to_f16_rne(v); break;
+    default: ((float*)base)[i] = v;
+  }
+}
+
 /* ---------------------------------------------------------------------------------- */
 /* u = q / max(||q||, eps)                                                             */
 /* The 64-element sum of squares follows the kernel's warp layout: lane l holds         */
@@ -134,6 +175,62 @@ void oracle_scores(const void* K, int dtype, int64_t k_stride_b, int64_t k_strid
     const int b = g / H_kv, hk = g % H_kv;
     score_group(K, dtype, (int64_t)b * k_stride_b + (int64_t)hk * k_stride_h,
                 u + (int64_t)g * G * ORACLE_D, G, N, scores + (int64_t)g * G * s_stride, s_stride);
+  }
+}
+
+/* ---------------------------------------------------------------------------------- */
+/* projected-score mode                                                                 */
+/* ---------------------------------------------------------------------------------- */
+HOT void oracle_project_keys(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
+                             int B, int H_kv, int N, const float* P, int R, void* KP,
+                             int64_t p_stride_b, int64_t p_stride_h) {
+#pragma omp parallel for schedule(static)
+  for (int g = 0; g < B * H_kv; ++g) {
+    const int b = g / H_kv, hk = g % H_kv;
+    const int64_t kb = (int64_t)b * k_stride_b + (int64_t)hk * k_stride_h;
+    const int64_t pb = (int64_t)b * p_stride_b + (int64_t)hk * p_stride_h;
+    float kr[ORACLE_D];
+    for (int n = 0; n < N; ++n) {
+      for (int d = 0; d < ORACLE_D; ++d) kr[d] = load_elem(K, dtype, kb + (int64_t)n * ORACLE_D + d);
+      for (int j = 0; j < R; ++j) {
+        float acc = 0.0f;
+        for (int d = 0; d < ORACLE_D; ++d) acc = fmaf(kr[d], P[d * R + j], acc);
+        store_elem(KP, dtype, pb + (int64_t)n * R + j, acc);
+      }
+    }
+  }
+}
+
+void oracle_query_projection(const float* u, int rows, const float* P, int R, float* qp) {
+  for (int r = 0; r < rows; ++r)
+    for (int j = 0; j < R; ++j) {
+      float acc = 0.0f;
+      for (int d = 0; d < ORACLE_D; ++d) acc = fmaf(u[(int64_t)r * ORACLE_D + d], P[d * R + j], acc);
+      qp[(int64_t)r * R + j] = acc;
+    }
+}
+
+HOT void oracle_scores_projected(const void* KP, int dtype, int64_t p_stride_b,
+                                 int64_t p_stride_h, const float* qp, int R, int B, int H,
+                                 int H_kv, int N, uint16_t* scores, int64_t s_stride) {
+  const int G = H / H_kv;
+#pragma omp parallel for schedule(static)
+  for (int g = 0; g < B * H_kv; ++g) {
+    const int b = g / H_kv, hk = g % H_kv;
+    const int64_t pb = (int64_t)b * p_stride_b + (int64_t)hk * p_stride_h;
+    float kr[64];
+    for (int n = 0; n < N; ++n) {
+      for (int j = 0; j < R; ++j) kr[j] = load_elem(KP, dtype, pb + (int64_t)n * R + j);
+      for (int h = 0; h < G; ++h) {
+        const float* q = qp + ((int64_t)g * G + h) * R;
+        float even = 0.0f, odd = 0.0f;
+        for (int j = 0; j < R; j += 2) {
+          even = fmaf(kr[j], q[j], even);
+          odd = fmaf(kr[j + 1], q[j + 1], odd);
+        }
+        scores[((int64_t)g * G + h) * s_stride + n] = f32_to_bf16_rne(even + odd);
+      }
+    }
   }
 }
 

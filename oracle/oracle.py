@@ -63,6 +63,14 @@ def _load():
         lib.oracle_attend.argtypes = [vp, vp, vp, i32, i64, i64, i64, i64, vp, i32, i32, i32,
                                       i32, i32, i32, vp]
         lib.oracle_attend.restype = None
+        lib.oracle_project_keys.argtypes = [vp, i32, i64, i64, i32, i32, i32, vp, i32, vp, i64,
+                                            i64]
+        lib.oracle_project_keys.restype = None
+        lib.oracle_query_projection.argtypes = [vp, i32, vp, i32, vp]
+        lib.oracle_query_projection.restype = None
+        lib.oracle_scores_projected.argtypes = [vp, i32, i64, i64, vp, i32, i32, i32, i32, i32,
+                                                vp, i64]
+        lib.oracle_scores_projected.restype = None
         lib.oracle_adaptive_k_window.argtypes = [i32, i32, ctypes.c_double]
         lib.oracle_adaptive_k_window.restype = i32
         _lib = lib
@@ -139,6 +147,55 @@ def decode(Q: np.ndarray, K: np.ndarray, V: np.ndarray, dtype: str, k: int,
     idx = select(s, k)
     O = attend(Q, K, V, dtype, idx)
     return u, s, idx, O
+
+
+# ---- projected-score mode (no counterpart in the reference) -------------------------
+def project_keys(K: np.ndarray, dtype: str, P: np.ndarray) -> np.ndarray:
+    """KP [B, H_kv, N, R] in K's storage (bits for 16-bit types): round(K . P)."""
+    K = _check(K, dtype)
+    P = np.ascontiguousarray(P, dtype=np.float32)
+    B, H_kv, N, D = K.shape
+    R = P.shape[1]
+    assert D == 64 and P.shape[0] == 64
+    KP = np.empty((B, H_kv, N, R), dtype=K.dtype)
+    _load().oracle_project_keys(_ptr(K), _DTYPES[dtype], H_kv * N * 64, N * 64, B, H_kv, N,
+                                _ptr(P), R, _ptr(KP), H_kv * N * R, N * R)
+    return KP
+
+
+def query_projection(u: np.ndarray, P: np.ndarray) -> np.ndarray:
+    """qp [..., R] = u . P (fp32)."""
+    u = np.ascontiguousarray(u, dtype=np.float32)
+    P = np.ascontiguousarray(P, dtype=np.float32)
+    R = P.shape[1]
+    rows = u.size // 64
+    qp = np.empty(u.shape[:-1] + (R,), dtype=np.float32)
+    _load().oracle_query_projection(_ptr(u), rows, _ptr(P), R, _ptr(qp))
+    return qp
+
+
+def scores_projected(KP: np.ndarray, dtype: str, qp: np.ndarray) -> np.ndarray:
+    """bf16 score bits [B*H, N] from KP [B, H_kv, N, R] and qp [B, H, R]."""
+    KP = _check(KP, dtype)
+    qp = np.ascontiguousarray(qp, dtype=np.float32)
+    B, H_kv, N, R = KP.shape
+    H = qp.shape[1]
+    out = np.empty((B * H, N), dtype=np.uint16)
+    _load().oracle_scores_projected(_ptr(KP), _DTYPES[dtype], H_kv * N * R, N * R, _ptr(qp), R,
+                                    B, H, H_kv, N, _ptr(out), N)
+    return out
+
+
+def decode_projected(Q, K, V, KP, P, dtype: str, k: int, eps: float = 1e-12):
+    """Projected-mode step: (qp, score bits, indices, fp32 output)."""
+    N = K.shape[2]
+    if N <= k:
+        raise ValueError(f"kernel invoked with N={N} <= k_eff={k}; caller must dispatch to SDPA")
+    qp = query_projection(unit_query(Q, dtype, eps), P)
+    s = scores_projected(KP, dtype, qp)
+    idx = select(s, k)
+    O = attend(Q, K, V, dtype, idx)
+    return qp, s, idx, O
 
 
 def adaptive_k_window(k_window_min: int, n_kv: int, coverage_floor: float) -> int:
