@@ -212,6 +212,54 @@ def test_peer_exchange_single_rank_steps(oracle_mod, cuda_lib):
     dec.close()
 
 
+def test_peer_wait_expires_and_reports(cuda_lib):
+    """Failure detection without a fault: a world-2 exchange in one process on one GPU
+    whose 'peer' buffer nothing writes. The step's first wait must give up after its bound,
+    raise DCR_ERR_DEVICE_TIMEOUT and set the abort word (every later wait returns at once),
+    and after dcr_xchg_reset the context and the buffers work again."""
+    import ctypes
+    import time
+    from dcr_b200 import _lib
+    from dcr_b200.sharded import CudaSequenceShardStep
+    from dcr_b200.synthetic import make_decode_inputs
+    lib = cuda_lib
+    B, H, H_kv, N, k = 1, 8, 2, 2048, 200
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=3, device=DEV)
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+    for b in bufs:
+        assert lib.dcr_xchg_create(B, H, 2, ctypes.byref(b), handle) == 0
+    peers = (ctypes.c_void_p * 2)(bufs[0].value, bufs[1].value)  # 'rank 1' never runs
+    step = CudaSequenceShardStep(B, H, H_kv, N, k, dtype=torch.bfloat16, device=DEV).bind(Q, K, V)
+    O = torch.empty(B, H, 64, dtype=torch.bfloat16, device=DEV)
+    assert _lib.read_device_status(clear=True) == 0
+    t0 = time.perf_counter()
+    st = lib.dcr_shard_decode_peer(Q.data_ptr(), K.data_ptr(), V.data_ptr(), 0, step.ksb,
+                                   step.ksh, step.vsb, step.vsh, B, H, H_kv, N, 64, k, 1e-12,
+                                   peers, 2, 0, O.data_ptr(), step.ws.data_ptr(), step.ws_bytes,
+                                   None)
+    assert st == 0
+    status = _lib.read_device_status(clear=True)       # synchronises
+    elapsed = time.perf_counter() - t0
+    assert status & _lib.DCR_ERR_DEVICE_TIMEOUT
+    assert 1.5 < elapsed < 30.0                         # one bounded wait, then the abort word
+    # after a reset of both buffers the single-rank step works again on the same context
+    for b in bufs:
+        assert lib.dcr_xchg_reset(b, B, H, 2, None) == 0
+        assert lib.dcr_xchg_destroy(b) == 0
+    one = ctypes.c_void_p()
+    assert lib.dcr_xchg_create(B, H, 1, ctypes.byref(one), handle) == 0
+    peers1 = (ctypes.c_void_p * 1)(one.value)
+    st = lib.dcr_shard_decode_peer(Q.data_ptr(), K.data_ptr(), V.data_ptr(), 0, step.ksb,
+                                   step.ksh, step.vsb, step.vsh, B, H, H_kv, N, 64, k, 1e-12,
+                                   peers1, 1, 0, O.data_ptr(), step.ws.data_ptr(),
+                                   step.ws_bytes, None)
+    assert st == 0
+    assert _lib.read_device_status(clear=True) == 0
+    assert torch.isfinite(O.float()).all()
+    assert lib.dcr_xchg_destroy(one) == 0
+
+
 # ---- two GPUs: the real NCCL path ------------------------------------------------------
 def _free_port() -> int:
     with socket.socket() as s:
