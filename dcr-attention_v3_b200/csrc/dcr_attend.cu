@@ -28,6 +28,10 @@
 // Every gathered index is checked against [0, N); a bad one is skipped (zero row, zero
 // weight) and raises DCR_ERR_DEVICE_INDEX.
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <type_traits>
 
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
@@ -66,6 +70,8 @@ struct P3Params {
   int* counters;
   PeerView pv;              // pv.world > 0 (with state): also copy each row's state into
                             // slot pv.rank of every peer's exchange buffer (exchange 2)
+  int64_t rows_per_head;    // TMA gather: cache rows of (b, h_kv) start at
+                            // (b * H_kv + h_kv) * rows_per_head in the 2-D tensor maps
 };
 
 // Writes a row's (m, l, o) to the state output and, in peer mode, to every peer's slot,
@@ -92,8 +98,14 @@ __device__ __forceinline__ void write_state_row(const P3Params& p, int64_t row, 
   row_pushed(p.pv, 2, p.pv.rows, step_epoch(p.pv));
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kernel(const P3Params p) {
+// kTma: the K and V rows of a tile are fetched by TMA gathers (tile::gather4, 4 rows per
+// instruction, issued by 16 lanes of warp 0) from 2-D tensor maps over the caches,
+// completing on one mbarrier per stage; otherwise by 16-byte cp.async copies of all
+// threads. Both write the same swizzled tile layout, and the arithmetic is identical.
+template <typename T, bool kTma>
+__global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
+    attend_kernel(const __grid_constant__ CUtensorMap kmap,
+                  const __grid_constant__ CUtensorMap vmap, const P3Params p) {
   using Cfg = P3Cfg<T>;
   constexpr int kChunks = Cfg::kChunks;
   constexpr int kPer = ElemTraits<T>::kPerChunk;
@@ -110,6 +122,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   __shared__ float m_red[kWarps];
   __shared__ float l_red[kWarps];
   __shared__ int is_last;
+  __shared__ alignas(8) uint64_t full_bar[Cfg::kStages];  // TMA: one per stage
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -152,16 +165,55 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   // Gather assignment: thread copies chunk `cchunk` of rows rbase + i * kRowsPerPass.
   const int cchunk = tid % kChunks;
   const int rbase = tid / kChunks;
+  const int64_t tma_row0 = (static_cast<int64_t>(b) * p.H_kv + hk) * p.rows_per_head;
+  if constexpr (kTma) {
+    if (tid == 0) {
+      tma_prefetch_desc(&kmap);
+      tma_prefetch_desc(&vmap);
+#pragma unroll
+      for (int i = 0; i < Cfg::kStages; ++i) mbar_init(&full_bar[i], 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+  }
 
   // Indices of the rows this thread copies in tile tt (-1: past the end of the list).
+  // TMA: lane l < 16 of warp 0 gathers rows 4l .. 4l + 3 of the tile.
   auto load_idx = [&](int tt, int32_t (&n)[kPasses]) {
 #pragma unroll
     for (int i = 0; i < kPasses; ++i) {
-      const int pos = tt * kP3Tile + rbase + i * kRowsPerPass;
-      n[i] = (pos < cnt) ? __ldg(idx_row + pos) : -1;
+      const int pos = kTma ? tt * kP3Tile + 4 * lane + i : tt * kP3Tile + rbase + i * kRowsPerPass;
+      const bool mine = !kTma || (warp == 0 && lane < kP3Tile / 4 && i < 4);
+      n[i] = (mine && pos < cnt) ? __ldg(idx_row + pos) : -1;
     }
   };
   auto issue = [&](int tt, const int32_t (&n)[kPasses]) {
+    if constexpr (kTma) {
+      if (tt < ntiles && warp == 0) {
+        const int stage = tt % Cfg::kStages;
+        uint8_t* kt = smem + stage * Cfg::kStageBytes;
+        uint8_t* vt = kt + Cfg::kTileBytes;
+        if (lane == 0) mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+        __syncwarp();
+        if (lane < kP3Tile / 4) {
+          int r[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            int nn = n[i];
+            if (nn < 0 || nn >= p.N) {
+              // past the list: any valid row (masked by `valid`); a bad index: row 0 of
+              // the head, reported
+              if (nn >= 0 || tt * kP3Tile + 4 * lane + i < cnt) raise_status(DCR_ERR_DEVICE_INDEX);
+              nn = 0;
+            }
+            r[i] = static_cast<int>(tma_row0 + nn);
+          }
+          tma_gather4(kt + 4 * lane * Cfg::kRowBytes, &kmap, &full_bar[stage], 0, r[0], r[1], r[2], r[3]);
+          tma_gather4(vt + 4 * lane * Cfg::kRowBytes, &vmap, &full_bar[stage], 0, r[0], r[1], r[2], r[3]);
+        }
+      }
+      return;
+    }
     if (tt < ntiles) {
       uint8_t* kt = smem + (tt % Cfg::kStages) * Cfg::kStageBytes;
       uint8_t* vt = kt + Cfg::kTileBytes;
@@ -206,7 +258,11 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   const int r_own = warp * 16 + (lane >> 1);
 
   for (int tt = 0; tt < ntiles; ++tt) {
-    cp_async_wait<Cfg::kStages - 2>();
+    if constexpr (kTma) {
+      mbar_wait_bounded(&full_bar[tt % Cfg::kStages], (tt / Cfg::kStages) & 1u);
+    } else {
+      cp_async_wait<Cfg::kStages - 2>();
+    }
     __syncthreads();  // tile tt visible to all; stage (tt-1) free for reuse
     issue(tt + Cfg::kStages - 1, n_next);
 #pragma unroll
@@ -281,7 +337,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks) attend_kerne
   }
   o0 += o0b;
   o1 += o1b;
-  cp_async_wait<0>();
+  if constexpr (!kTma) cp_async_wait<0>();
 
   // ---- merge the 4 warps' (m, l, o) ----
   float ls = l_part;
@@ -361,14 +417,66 @@ int attend_splits(int rows, int k_eff) {
   return S;
 }
 
+// TMA gathers need one row index space per cache: rows of (b, h_kv) at a fixed pitch
+// (batch stride = H_kv x head stride, head stride a whole number of rows, K and V alike),
+// 16-bit elements (a 128-byte row is one swizzle span) and int32 row indices. They are
+// opt-in (DCR_ATTEND_GATHER=tma in the environment): at the hero shape the 16-byte
+// cp.async path is faster (35 us against 45 us per launch), the TMA unit's rate for
+// 128-byte rows being lower than the load units' for the same bytes.
+static bool tma_gather_allowed() {
+  static const bool allowed = [] {
+    const char* e = getenv("DCR_ATTEND_GATHER");
+    return e != nullptr && strcmp(e, "tma") == 0;
+  }();
+  return allowed;
+}
+
 template <typename T>
-static int launch_attend_t(const P3Params& p, int B, cudaStream_t st) {
-  constexpr int smem = P3Cfg<T>::kSmem;
-  if (ensure_smem_attr(reinterpret_cast<const void*>(&attend_kernel<T>), smem) != cudaSuccess)
-    return DCR_ERR_CUDA;
+static bool encode_row_map(CUtensorMap* map, const void* base, int64_t rows) {
+  EncodeTiledFn encode = get_encode_fn();
+  if (!encode) return false;
+  const CUtensorMapDataType dt = std::is_same<T, __half>::value
+                                     ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                     : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kD * sizeof(T))};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kD), 1u};  // gather4: one row high
+  const cuuint32_t estr[2] = {1u, 1u};
+  return encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T>
+static int launch_attend_t(P3Params p, int B, cudaStream_t st) {
   const int64_t grid = static_cast<int64_t>(B) * p.H_kv * p.S * p.G;
   if (grid > 0x7fffffff) return DCR_ERR_SHAPE;
-  attend_kernel<T><<<static_cast<unsigned>(grid), kP3Threads, smem, st>>>(p);
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  bool tma = false;
+  if constexpr (sizeof(T) == 2) {
+    const int64_t rph = p.ksh / kD;
+    const int64_t rows = static_cast<int64_t>(B) * p.H_kv * rph;
+    tma = tma_gather_allowed() && p.ksh % kD == 0 && p.ksh == p.vsh && p.ksb == p.vsb &&
+          (B == 1 || p.ksb == p.H_kv * p.ksh) && rows > 0 && rows <= 0x7fffffffLL &&
+          encode_row_map<T>(&kmap, p.k, rows) && encode_row_map<T>(&vmap, p.v, rows);
+    p.rows_per_head = rph;
+    if (tma) {
+      constexpr int smem = P3Cfg<T>::kSmem;
+      if (ensure_smem_attr(reinterpret_cast<const void*>(&attend_kernel<T, true>), smem) !=
+          cudaSuccess)
+        return DCR_ERR_CUDA;
+      attend_kernel<T, true><<<static_cast<unsigned>(grid), kP3Threads, smem, st>>>(kmap, vmap, p);
+      return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+    }
+  }
+  constexpr int smem = P3Cfg<T>::kSmem;
+  if (ensure_smem_attr(reinterpret_cast<const void*>(&attend_kernel<T, false>), smem) !=
+      cudaSuccess)
+    return DCR_ERR_CUDA;
+  attend_kernel<T, false><<<static_cast<unsigned>(grid), kP3Threads, smem, st>>>(kmap, vmap, p);
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }
 
@@ -397,6 +505,7 @@ int launch_attend(const void* Q, const void* K, const void* V, int dtype, int64_
   p.state = state;
   p.pv.world = 0;
   if (pv != nullptr) p.pv = *pv;
+  p.rows_per_head = 0;
   p.part = partials;
   p.counters = counters;
   switch (dtype) {

@@ -182,6 +182,19 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
+// TMA gather of 4 rows (tile::gather4; the 2-D tensor map's box is one row high): rows
+// r0..r3, columns [x, x + box width), written one after another at smem_dst (with the
+// map's swizzle); completes on an mbarrier. No multicast.
+__device__ __forceinline__ void tma_gather4(void* smem_dst, const void* tmap, uint64_t* bar,
+                                            int x, int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1),
+      "r"(r2), "r"(r3)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }

@@ -84,12 +84,14 @@ __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p)
   const int nvec = (N + 7) >> 3;
   const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
 
-  uint32_t* hist_hi0 = cluster.map_shared_rank(hist_hi, 0);
-  uint32_t* hist_lo0 = cluster.map_shared_rank(hist_lo, 0);
+  // CTA 0's copies (its own shared memory when the row has one CTA)
+  const bool clustered = C > 1;
+  uint32_t* hist_hi0 = clustered ? cluster.map_shared_rank(hist_hi, 0) : hist_hi;
+  uint32_t* hist_lo0 = clustered ? cluster.map_shared_rank(hist_lo, 0) : hist_lo;
   uint32_t* gt0 = cluster.map_shared_rank(cta_gt, 0);
   uint32_t* eq0 = cluster.map_shared_rank(cta_eq, 0);
-  int* bh0 = cluster.map_shared_rank(&s_bh, 0);
-  uint32_t* above0 = cluster.map_shared_rank(&s_above, 0);
+  int* bh0 = clustered ? cluster.map_shared_rank(&s_bh, 0) : &s_bh;
+  uint32_t* above0 = clustered ? cluster.map_shared_rank(&s_above, 0) : &s_above;
 
   if (crank == 0 && tid == 0 && p.row_counters != nullptr) p.row_counters[row] = 0;
   if (tid < 256) {

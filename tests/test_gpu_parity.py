@@ -11,6 +11,8 @@ and the size-independent properties of an exact top-K are checked on the device.
 """
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -281,3 +283,44 @@ def test_full_size_vs_oracle(oracle_mod, B, H, H_kv, N, c, dt):
     assert np.array_equal(idx.cpu().numpy().reshape(B * H, k), idx_o)
     ok, st = attention_close(O, O_o, got_rounded_to=dt)
     assert ok, st
+
+
+_GATHER_SCRIPT = r"""
+import os, sys
+sys.path[:0] = [sys.argv[2], os.path.join(sys.argv[2], "dcr-attention_v3_b200")]
+import torch
+from dcr_b200.kernel.cuda import topk_qaxis_attention
+from dcr_b200.synthetic import make_decode_inputs
+dev = torch.device("cuda:0")
+outs = []
+for dt, (B, H, H_kv, N, k) in [(torch.float16, (2, 32, 8, 5000, 750)),
+                              (torch.bfloat16, (1, 16, 2, 3001, 450))]:
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=dt, seed=31, device=dev)
+    outs.append(topk_qaxis_attention(Q, K, V, k).cpu())
+    big = torch.zeros(B, H_kv, N + 77, 64, dtype=dt, device=dev)     # cache for N_max positions
+    big[:, :, :N] = K
+    bigv = torch.zeros_like(big)
+    bigv[:, :, :N] = V
+    outs.append(topk_qaxis_attention(Q, big[:, :, :N], bigv[:, :, :N], k).cpu())
+torch.save(outs, sys.argv[1])
+"""
+
+
+def test_tma_gather_matches_cp_async(tmp_path):
+    """Pass 3's two row-fetch paths (16-byte cp.async, the default, and the opt-in TMA
+    gather4 for 16-bit caches with a uniform row pitch) give bit-identical outputs."""
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    script = tmp_path / "gather.py"
+    script.write_text(_GATHER_SCRIPT)
+    res = {}
+    for mode in ("tma", "cpasync"):
+        env = dict(os.environ)
+        env["DCR_ATTEND_GATHER"] = mode
+        out = tmp_path / f"{mode}.pt"
+        subprocess.run([sys.executable, str(script), str(out), root], env=env, check=True,
+                       timeout=300)
+        res[mode] = torch.load(out)
+    for a, b in zip(res["tma"], res["cpasync"]):
+        assert torch.equal(a, b)
