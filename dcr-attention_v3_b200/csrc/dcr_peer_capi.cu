@@ -126,12 +126,20 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
                          reinterpret_cast<uint16_t*>(ws + w.scores), w.n_pad, 1, s)))
     return st;
   if ((st = mark(1))) return st;
-  if ((st = launch_shard_hist(w, ws, rows, N_local, k_eff, 0, nullptr, nullptr, &v, s))) return st;
-  if ((st = mark(2))) return st;
-  if ((st = launch_shard_hist(w, ws, rows, N_local, k_eff, 1, nullptr, nullptr, &v, s))) return st;
-  if ((st = mark(3))) return st;
-  if ((st = launch_shard_select(w, ws, rows, N_local, k_eff, nullptr, world, rank, &v, s)))
-    return st;
+  bool fused = false;
+  if ((st = launch_shard_select_fused(w, ws, rows, N_local, k_eff, &v, s, &fused))) return st;
+  if (fused) {
+    if ((st = mark(2)) || (st = mark(3))) return st;
+  } else {
+    if ((st = launch_shard_hist(w, ws, rows, N_local, k_eff, 0, nullptr, nullptr, &v, s)))
+      return st;
+    if ((st = mark(2))) return st;
+    if ((st = launch_shard_hist(w, ws, rows, N_local, k_eff, 1, nullptr, nullptr, &v, s)))
+      return st;
+    if ((st = mark(3))) return st;
+    if ((st = launch_shard_select(w, ws, rows, N_local, k_eff, nullptr, world, rank, &v, s)))
+      return st;
+  }
   if ((st = mark(4))) return st;
   float* own_state = reinterpret_cast<float*>(v.base[rank] + v.lay.st) +
                      static_cast<int64_t>(rank) * rows * kStateFloats;

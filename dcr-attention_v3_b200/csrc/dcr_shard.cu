@@ -351,6 +351,199 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
   }
 }
 
+// Fused selection of the peer-exchange step (kernels above, phases 1-3b, in one launch):
+// one 512-thread CTA per row holds the row's keys in registers (up to 64 per thread)
+// through both histogram exchanges. The CTA publishes its row's high-byte histogram into
+// its own slot and every peer's (exchange 0), waits for the peers', finds BH, publishes
+// the low-byte histogram of its keys in BH (exchange 1), waits, finds T and its tie
+// quota, and emits its positions as Pass 2 does. Launched cooperatively (every row's CTA
+// resident), so a CTA that waits for the exchange's last row never waits for a CTA that
+// has not started. The own slots are left zero for the accumulating phase kernels.
+constexpr int kFsThreads = 512;
+constexpr int kFsWarps = kFsThreads / 32;
+
+template <int VPT>
+__global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const ShardParams p) {
+  constexpr int kKeys = VPT * 8;
+  constexpr int kWords = (kKeys + 31) / 32;
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t hsum[256];
+  __shared__ uint32_t wsum[kFsWarps];
+  __shared__ uint32_t s_bh, s_above, s_T, s_quota, s_tot;
+  const PeerView& v = p.v;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t row = blockIdx.x;
+  const int rank = v.rank;
+  const uint32_t epoch = step_epoch(v);
+  if (tid < 256) hist[tid] = 0u;
+
+  // keys of this thread: positions [v0 * 8, (v0 + VPT) * 8); 0 past the row
+  const uint16_t* src = p.keys + row * p.stride;
+  const int v0 = tid * VPT;
+  uint32_t key[kKeys];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int base = (v0 + j) * 8;
+    if (base + 8 <= p.N) {
+      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(src + base));
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        key[8 * j + 2 * i] = ww[i] & 0xffffu;
+        key[8 * j + 2 * i + 1] = ww[i] >> 16;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) key[8 * j + e] = (base + e < p.N) ? src[base + e] : 0u;
+    }
+  }
+  __syncthreads();
+
+  // ---- exchange 0: high-byte histograms ----
+#pragma unroll
+  for (int e = 0; e < kKeys; ++e)
+    if (key[e] != 0u) atomicAdd(&hist[key[e] >> 8], 1u);
+  __syncthreads();
+  if (tid < 256) {
+    const int32_t c = static_cast<int32_t>(hist[tid]);
+    for (int q = 0; q < v.world; ++q) v.hh(q, rank, row)[tid] = c;  // own slot included
+  }
+  row_pushed(v, 0, p.rows, epoch);
+  if (warp == 0) wait_peers(v, 0, epoch);
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t sum = 0;
+    for (int r = 0; r < v.world; ++r) sum += static_cast<uint32_t>(__ldcg(v.hh(rank, r, row) + tid));
+    hsum[tid] = sum;
+    hist[tid] = 0u;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int bin;
+    uint32_t above;
+    warp_find_bin(hsum, static_cast<uint32_t>(p.k), bin, above);
+    if (lane == 0) {
+      if (bin < 0) {
+        raise_status(DCR_ERR_DEVICE_SHARD);
+        bin = 0;
+        above = 0;
+      }
+      s_bh = static_cast<uint32_t>(bin);
+      s_above = above;
+      p.row_state[row * 4 + 0] = bin;
+      p.row_state[row * 4 + 1] = static_cast<int32_t>(above);
+    }
+  }
+  __syncthreads();
+
+  // ---- exchange 1: low-byte histograms of the keys in BH ----
+  const uint32_t bh = s_bh;
+#pragma unroll
+  for (int e = 0; e < kKeys; ++e)
+    if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist[key[e] & 0xffu], 1u);
+  __syncthreads();
+  if (tid < 256) {
+    const int32_t c = static_cast<int32_t>(hist[tid]);
+    for (int q = 0; q < v.world; ++q) v.hl(q, rank, row)[tid] = c;
+    v.hh(rank, rank, row)[tid] = 0;  // own high-byte slot no longer read
+  }
+  row_pushed(v, 1, p.rows, epoch);
+  if (warp == 0) wait_peers(v, 1, epoch);
+  __syncthreads();
+  if (tid < 256) {
+    uint32_t sum = 0;
+    for (int r = 0; r < v.world; ++r) sum += static_cast<uint32_t>(__ldcg(v.hl(rank, r, row) + tid));
+    hsum[tid] = sum;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int bl;
+    uint32_t above_lo;
+    warp_find_bin(hsum, static_cast<uint32_t>(p.k) - s_above, bl, above_lo);
+    if (lane == 0) {
+      if (bl < 0) {
+        raise_status(DCR_ERR_DEVICE_SHARD);
+        bl = 0;
+        above_lo = 0;
+      }
+      const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
+      const int need = p.k - static_cast<int>(s_above + above_lo);
+      int eq_lower = 0;
+      for (int r = 0; r < rank; ++r) eq_lower += __ldcg(v.hl(rank, r, row) + bl);
+      const int eq_mine = static_cast<int>(hist[bl]);
+      s_T = T;
+      s_quota = static_cast<uint32_t>(max(0, min(need - eq_lower, eq_mine)));
+      p.row_state[row * 4 + 2] = static_cast<int32_t>(T);
+      p.row_state[row * 4 + 3] = static_cast<int32_t>(s_quota);
+    }
+  }
+  __syncthreads();
+  if (tid < 256) v.hl(rank, rank, row)[tid] = 0;  // own low-byte slot no longer read
+  const uint32_t T = s_T;
+  const int quota = static_cast<int>(s_quota);
+
+  // ---- masks, block scan, ordered emission (as Pass 2) ----
+  uint32_t gtm[kWords], eqm[kWords];
+#pragma unroll
+  for (int w = 0; w < kWords; ++w) gtm[w] = eqm[w] = 0u;
+#pragma unroll
+  for (int e = 0; e < kKeys; ++e) {
+    gtm[e >> 5] |= (key[e] > T ? 1u : 0u) << (e & 31);
+    eqm[e >> 5] |= (key[e] == T ? 1u : 0u) << (e & 31);
+  }
+  uint32_t ngt = 0, neq = 0;
+#pragma unroll
+  for (int w = 0; w < kWords; ++w) {
+    ngt += __popc(gtm[w]);
+    neq += __popc(eqm[w]);
+  }
+  const uint32_t packed = ngt | (neq << 16);
+  const uint32_t incl = warp_incl_scan(packed);
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const uint32_t ws = lane < kFsWarps ? wsum[lane] : 0u;
+    const uint32_t wi = warp_incl_scan(ws);
+    if (lane < kFsWarps) wsum[lane] = wi - ws;
+    if (lane == kFsWarps - 1) s_tot = wi;
+  }
+  __syncthreads();
+  const uint32_t ex = incl - packed + wsum[warp];
+  const int eq_before = static_cast<int>(ex >> 16);
+  int pos = static_cast<int>(ex & 0xffffu) + min(eq_before, quota);
+  int take = quota - eq_before;
+  int32_t* out = p.idx + row * p.cap;
+  const int base = v0 * 8;
+#pragma unroll
+  for (int w = 0; w < kWords; ++w) {
+    uint32_t sel = gtm[w];
+    const uint32_t eq = eqm[w];
+    const int neq_w = __popc(eq);
+    if (take >= neq_w) {
+      sel |= eq;
+      take -= neq_w;
+    } else if (take > 0) {
+      uint32_t rem = eq;
+      for (int i = 0; i < take; ++i) rem &= rem - 1;
+      sel |= eq & ~rem;
+      take = 0;
+    }
+    while (sel) {
+      const int bb = __ffs(sel) - 1;
+      sel &= sel - 1;
+      if (pos < p.cap) out[pos] = base + 32 * w + bb;
+      else raise_status(DCR_ERR_DEVICE_SHARD);
+      ++pos;
+    }
+  }
+  if (tid == 0) {
+    p.count[row] = min(static_cast<int>(s_tot & 0xffffu) + quota, p.cap);
+    p.counters[row] = 0;
+  }
+}
+
 size_t align_up_256(size_t x) { return (x + 255) / 256 * 256; }
 
 ShardLayout shard_layout(int rows, int N_local, int k_eff) {
@@ -435,6 +628,45 @@ int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local
   if (e) return e;
   shard_emit_kernel<<<static_cast<unsigned>(grid), kShThreads, 0, st>>>(p);
   return check_launch();
+}
+
+template <int VPT>
+static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, shard_select_fused_kernel<VPT>,
+                                                    kFsThreads, 0) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_OK;  // not resident
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.rows));
+  cfg.blockDim = dim3(kFsThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, shard_select_fused_kernel<VPT>, p) != cudaSuccess)
+    return DCR_ERR_CUDA;
+  *launched = true;
+  return DCR_OK;
+}
+
+int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
+                              int k_eff, const PeerView* pv, cudaStream_t st, bool* launched) {
+  *launched = false;
+  const int nvec = (N_local + 7) / 8;
+  if (pv == nullptr || nvec > kFsThreads * 8) return DCR_OK;
+  ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
+  p.v = *pv;
+  p.world = pv->world;
+  p.rank = pv->rank;
+  const int vpt = (nvec + kFsThreads - 1) / kFsThreads;
+  if (vpt <= 1) return launch_fused_t<1>(p, st, launched);
+  if (vpt <= 2) return launch_fused_t<2>(p, st, launched);
+  if (vpt <= 4) return launch_fused_t<4>(p, st, launched);
+  return launch_fused_t<8>(p, st, launched);
 }
 
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
