@@ -68,40 +68,38 @@ struct P3Params {
   float* state;             // optional [rows][D + 2]: (m, l, o) instead of O
   float* part;
   int* counters;
-  PeerView pv;              // pv.world > 0 (with state): also copy each row's state into
-                            // slot pv.rank of every peer's exchange buffer (exchange 2)
+  PeerView pv;              // pv.world > 0 (with state): publish each row's state into
+                            // the ranks' exchange buffers instead (exchange 2)
   int64_t rows_per_head;    // TMA gather: cache rows of (b, h_kv) start at
                             // (b * H_kv + h_kv) * rows_per_head in the 2-D tensor maps
 };
 
-// Writes a row's (m, l, o) to the state output and, in peer mode, to every peer's slot,
-// then releases the peers' flag. Called by all threads of the CTA; threads 0..D-1 hold o.
+// Writes a row's (m, l, o) to the state output, or in peer mode publishes it into slot
+// `rank` of every rank's exchange buffer as epoch-tagged words. Called by all threads of
+// the CTA; threads 0..D-1 hold o, thread 0 holds m and l.
 __device__ __forceinline__ void write_state_row(const P3Params& p, int64_t row, float m, float l,
                                                 float o) {
   const int tid = threadIdx.x;
+  if (p.pv.world > 0) {
+    const uint32_t epoch = step_epoch(p.pv);
+    for (int q = 0; q < p.pv.world; ++q) {
+      uint64_t* dst = p.pv.st(q, p.pv.rank, row);
+      if (tid < kD) ll_put(dst + 2 + tid, __float_as_uint(o), epoch);
+      if (tid == 0) {
+        ll_put(dst, __float_as_uint(m), epoch);
+        ll_put(dst + 1, __float_as_uint(l), epoch);
+      }
+    }
+    return;
+  }
   float* st = p.state + row * (kD + 2);
   if (tid < kD) st[2 + tid] = o;
   if (tid == 0) {
     st[0] = m;
     st[1] = l;
   }
-  if (p.pv.world <= 0) return;
-  for (int q = 0; q < p.pv.world; ++q) {
-    if (q == p.pv.rank) continue;
-    float* dst = p.pv.st(q, p.pv.rank, row);
-    if (tid < kD) dst[2 + tid] = o;
-    if (tid == 0) {
-      dst[0] = m;
-      dst[1] = l;
-    }
-  }
-  row_pushed(p.pv, 2, p.pv.rows, step_epoch(p.pv));
 }
 
-// kTma: the K and V rows of a tile are fetched by TMA gathers (tile::gather4, 4 rows per
-// instruction, issued by 16 lanes of warp 0) from 2-D tensor maps over the caches,
-// completing on one mbarrier per stage; otherwise by 16-byte cp.async copies of all
-// threads. Both write the same swizzled tile layout, and the arithmetic is identical.
 template <typename T, bool kTma>
 __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
     attend_kernel(const __grid_constant__ CUtensorMap kmap,

@@ -141,8 +141,9 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
       return st;
   }
   if ((st = mark(4))) return st;
-  float* own_state = reinterpret_cast<float*>(v.base[rank] + v.lay.st) +
-                     static_cast<int64_t>(rank) * rows * kStateFloats;
+  // Pass 3 publishes its states into the exchange buffers; the pointer only selects the
+  // state output
+  float* own_state = reinterpret_cast<float*>(v.base[rank] + v.lay.st);
   if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
                           reinterpret_cast<const int32_t*>(ws + w.idx),
                           reinterpret_cast<const int32_t*>(ws + w.count), B, H, H_kv, N_local,

@@ -87,9 +87,10 @@ __device__ __forceinline__ void shard_load_keys(const ShardParams& p, int64_t ro
 
 // Phase 1 (kLevel 0): histogram of key >> 8. Phase 2 (kLevel 1): find BH in the global
 // high-byte histogram, then histogram key & 0xff over the keys in BH.
-// Peer mode: the row's histogram accumulates in this rank's own slot; the last CTA of the
-// row copies it to the peers' buffers and releases their flag (exchange kLevel). Phase 2
-// first waits for the peers' high-byte rows and sums the slots.
+// Peer mode: the row's histogram accumulates in this rank's accumulator; the last CTA of
+// the row publishes it into slot `rank` of every rank's buffer as epoch-tagged words
+// (exchange kLevel) and clears the accumulator. Phase 2 first reads every rank's
+// high-byte row (waiting for each word's epoch) and sums them.
 template <int kLevel>
 __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParams p) {
   __shared__ uint32_t h[256];
@@ -105,11 +106,8 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   if (kLevel == 1) {
     const uint32_t* hist_hi = reinterpret_cast<const uint32_t*>(p.hist_hi + row * 256);
     if (peer) {
-      if (tid < 32) wait_peers(p.v, 0, epoch);
-      __syncthreads();
       uint32_t sum = 0;
-      for (int r = 0; r < p.v.world; ++r)
-        sum += static_cast<uint32_t>(__ldcg(p.v.hh(p.v.rank, r, row) + tid));
+      for (int r = 0; r < p.v.world; ++r) sum += ll_get(p.v, p.v.hh(p.v.rank, r, row) + tid, epoch);
       hsum[tid] = sum;
       __syncthreads();
       hist_hi = hsum;
@@ -147,8 +145,7 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   }
   __syncthreads();
   const uint32_t c = h[tid];
-  int32_t* dst = p.hist_out + row * 256;
-  if (peer) dst = kLevel ? p.v.hl(p.v.rank, p.v.rank, row) : p.v.hh(p.v.rank, p.v.rank, row);
+  int32_t* dst = peer ? p.v.acc(kLevel, row) : p.hist_out + row * 256;
   if (c) atomicAdd(reinterpret_cast<unsigned int*>(dst + tid), c);
   if (!peer) return;
   __syncthreads();
@@ -159,14 +156,11 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   }
   __syncthreads();
   if (!s_last) return;
-  const int32_t val = __ldcg(dst + tid);
-  for (int q = 0; q < p.v.world; ++q) {
-    if (q == p.v.rank) continue;
-    int32_t* peer_dst = kLevel ? p.v.hl(q, p.v.rank, row) : p.v.hh(q, p.v.rank, row);
-    peer_dst[tid] = val;
-  }
+  const uint32_t val = static_cast<uint32_t>(__ldcg(dst + tid));
+  dst[tid] = 0;  // every chunk CTA of the row has added: clear for the next step
+  for (int q = 0; q < p.v.world; ++q)
+    ll_put((kLevel ? p.v.hl(q, p.v.rank, row) : p.v.hh(q, p.v.rank, row)) + tid, val, epoch);
   if (tid == 0) *p.v.ticket(kLevel, row) = 0u;
-  row_pushed(p.v, kLevel, p.rows, epoch);
 }
 
 // Phase 3a: T and this rank's tie quota from the gathered low-byte histograms; per-chunk
@@ -182,18 +176,16 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
   const int chunk = blockIdx.x % p.chunks;
   const uint32_t bh = static_cast<uint32_t>(p.row_state[row * 4 + 0]);
   const uint32_t above = static_cast<uint32_t>(p.row_state[row * 4 + 1]);
-  const int32_t* lo_all = p.hist_lo_all;
-  if (p.v.world > 0) {
-    // the peers' low-byte rows land in this rank's hl slots ([world][rows][256] like
-    // hist_lo_all); this rank's own high-byte slot is free again for the next step
-    if (warp == 0) wait_peers(p.v, 1, step_epoch(p.v));
-    if (chunk == 0) p.v.hh(p.v.rank, p.v.rank, row)[tid] = 0;
-    __syncthreads();
-    lo_all = reinterpret_cast<const int32_t*>(p.v.base[p.v.rank] + p.v.lay.hl);
-  }
+  const bool peer = p.v.world > 0;
+  const uint32_t epoch = peer ? step_epoch(p.v) : 0u;
+  // rank r's low-byte count of bin b: its published word (peer mode) or hist_lo_all
+  auto lo = [&](int r, int b) -> uint32_t {
+    if (peer) return ll_get(p.v, p.v.hl(p.v.rank, r, row) + b, epoch);
+    return static_cast<uint32_t>(
+        __ldcg(p.hist_lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + b));
+  };
   uint32_t tot = 0;
-  for (int r = 0; r < p.world; ++r)
-    tot += static_cast<uint32_t>(__ldcg(lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + tid));
+  for (int r = 0; r < p.world; ++r) tot += lo(r, tid);
   h[tid] = tot;
   uint32_t key[kShKeys];
   shard_load_keys(p, row, chunk, key);
@@ -211,9 +203,8 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
       const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
       const int need = p.k - static_cast<int>(above + above_lo);
       int eq_lower = 0;
-      for (int r = 0; r < p.rank; ++r)
-        eq_lower += __ldcg(lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + bl);
-      const int eq_mine = __ldcg(lo_all + (static_cast<int64_t>(p.rank) * p.rows + row) * 256 + bl);
+      for (int r = 0; r < p.rank; ++r) eq_lower += static_cast<int>(lo(r, bl));
+      const int eq_mine = static_cast<int>(lo(p.rank, bl));
       const int quota = max(0, min(need - eq_lower, eq_mine));
       s_T = T;
       if (chunk == 0) {
@@ -311,34 +302,30 @@ __global__ void __launch_bounds__(kShThreads) shard_emit_kernel(const ShardParam
     p.count[row] = static_cast<int32_t>(min(s_gt_all + quota, static_cast<uint32_t>(p.cap)));
     p.counters[row] = 0;
   }
-  if (p.v.world > 0 && chunk == 0) p.v.hl(p.v.rank, p.v.rank, row)[tid] = 0;  // read by phase 3a
 }
 
-// Phase 4: merge the ranks' (m, l, o) states of a row into O. Peer mode: wait for the
-// peers' states of the row, read them from this rank's slots, and let the last CTA
-// advance the epoch (the step is complete on this rank).
+// Phase 4: merge the ranks' (m, l, o) states of a row into O. Peer mode: read every
+// rank's state words of the row from this rank's slots (waiting for their epoch), and
+// let the last CTA advance the epoch (the step is complete on this rank).
 template <typename T>
 __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, int world,
                                                            int rows, void* O, const PeerView v) {
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
-  uint32_t epoch = 0;
-  if (v.world > 0) {
-    epoch = step_epoch(v);
-    if (tid < 32) wait_peers(v, 2, epoch);
-    __syncthreads();
-    states = reinterpret_cast<const float*>(v.base[v.rank] + v.lay.st);
-  }
+  const uint32_t epoch = v.world > 0 ? step_epoch(v) : 0u;
+  // word i of rank r's state of this row
+  auto state = [&](int r, int i) -> float {
+    if (v.world > 0) return __uint_as_float(ll_get(v, v.st(v.rank, r, row) + i, epoch));
+    return __ldcg(states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats + i);
+  };
   float M = -INFINITY;
-  for (int r = 0; r < world; ++r)
-    M = fmaxf(M, __ldcg(states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats));
+  for (int r = 0; r < world; ++r) M = fmaxf(M, state(r, 0));
   float L = 0.0f, o = 0.0f;
   for (int r = 0; r < world; ++r) {
-    const float* st = states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats;
-    const float m = __ldcg(st);
+    const float m = state(r, 0);
     const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
-    L = fmaf(w, __ldcg(st + 1), L);
-    o = fmaf(w, __ldcg(st + 2 + tid), o);
+    L = fmaf(w, state(r, 1), L);
+    o = fmaf(w, state(r, 2 + tid), o);
   }
   ElemTraits<T>::store(O, static_cast<int>(row * kD + tid), o / L);
   if (v.world > 0) {
@@ -354,11 +341,11 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
 // Fused selection of the peer-exchange step (kernels above, phases 1-3b, in one launch):
 // one 512-thread CTA per row holds the row's keys in registers (up to 64 per thread)
 // through both histogram exchanges. The CTA publishes its row's high-byte histogram into
-// its own slot and every peer's (exchange 0), waits for the peers', finds BH, publishes
-// the low-byte histogram of its keys in BH (exchange 1), waits, finds T and its tie
-// quota, and emits its positions as Pass 2 does. Launched cooperatively (every row's CTA
-// resident), so a CTA that waits for the exchange's last row never waits for a CTA that
-// has not started. The own slots are left zero for the accumulating phase kernels.
+// slot `rank` of every rank's buffer (exchange 0), reads every rank's row as its words
+// arrive, finds BH, publishes the low-byte histogram of its keys in BH (exchange 1),
+// reads, finds T and its tie quota, and emits its positions as Pass 2 does. Each row
+// waits only for the same row of the other ranks; the launch is cooperative (every row's
+// CTA resident) so that no row waits behind a CTA that cannot start.
 constexpr int kFsThreads = 512;
 constexpr int kFsWarps = kFsThreads / 32;
 
@@ -407,15 +394,10 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
     if (key[e] != 0u) atomicAdd(&hist[key[e] >> 8], 1u);
   __syncthreads();
   if (tid < 256) {
-    const int32_t c = static_cast<int32_t>(hist[tid]);
-    for (int q = 0; q < v.world; ++q) v.hh(q, rank, row)[tid] = c;  // own slot included
-  }
-  row_pushed(v, 0, p.rows, epoch);
-  if (warp == 0) wait_peers(v, 0, epoch);
-  __syncthreads();
-  if (tid < 256) {
+    const uint32_t c = hist[tid];
+    for (int q = 0; q < v.world; ++q) ll_put(v.hh(q, rank, row) + tid, c, epoch);  // own too
     uint32_t sum = 0;
-    for (int r = 0; r < v.world; ++r) sum += static_cast<uint32_t>(__ldcg(v.hh(rank, r, row) + tid));
+    for (int r = 0; r < v.world; ++r) sum += ll_get(v, v.hh(rank, r, row) + tid, epoch);
     hsum[tid] = sum;
     hist[tid] = 0u;
   }
@@ -445,16 +427,10 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
     if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist[key[e] & 0xffu], 1u);
   __syncthreads();
   if (tid < 256) {
-    const int32_t c = static_cast<int32_t>(hist[tid]);
-    for (int q = 0; q < v.world; ++q) v.hl(q, rank, row)[tid] = c;
-    v.hh(rank, rank, row)[tid] = 0;  // own high-byte slot no longer read
-  }
-  row_pushed(v, 1, p.rows, epoch);
-  if (warp == 0) wait_peers(v, 1, epoch);
-  __syncthreads();
-  if (tid < 256) {
+    const uint32_t c = hist[tid];
+    for (int q = 0; q < v.world; ++q) ll_put(v.hl(q, rank, row) + tid, c, epoch);
     uint32_t sum = 0;
-    for (int r = 0; r < v.world; ++r) sum += static_cast<uint32_t>(__ldcg(v.hl(rank, r, row) + tid));
+    for (int r = 0; r < v.world; ++r) sum += ll_get(v, v.hl(rank, r, row) + tid, epoch);
     hsum[tid] = sum;
   }
   __syncthreads();
@@ -471,7 +447,7 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
       const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
       const int need = p.k - static_cast<int>(s_above + above_lo);
       int eq_lower = 0;
-      for (int r = 0; r < rank; ++r) eq_lower += __ldcg(v.hl(rank, r, row) + bl);
+      for (int r = 0; r < rank; ++r) eq_lower += static_cast<int>(ll_get(v, v.hl(rank, r, row) + bl, epoch));
       const int eq_mine = static_cast<int>(hist[bl]);
       s_T = T;
       s_quota = static_cast<uint32_t>(max(0, min(need - eq_lower, eq_mine)));
@@ -480,7 +456,6 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
     }
   }
   __syncthreads();
-  if (tid < 256) v.hl(rank, rank, row)[tid] = 0;  // own low-byte slot no longer read
   const uint32_t T = s_T;
   const int quota = static_cast<int>(s_quota);
 
