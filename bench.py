@@ -677,7 +677,7 @@ def run_sharded_arm(args):
             code = st.lib.dcr_shard_decode_peer_timed(
                 st.Q.data_ptr(), st.K.data_ptr(), st.V.data_ptr(), st.dt, st.ksb, st.ksh,
                 st.vsb, st.vsh, st.B, st.H, st.H_kv, st.N, D, st.k, st.eps, px.peers,
-                px.world, px.rank, O.data_ptr(), st.ws.data_ptr(), st.ws_bytes,
+                px.world, px.rank, max(dec.n_locals), O.data_ptr(), st.ws.data_ptr(), st.ws_bytes,
                 stream.cuda_stream, arr)
             if code:
                 raise _lib.DCRError(code, "dcr_shard_decode_peer_timed")

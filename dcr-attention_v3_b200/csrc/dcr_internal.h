@@ -102,11 +102,13 @@ int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local
                         const struct PeerView* pv, cudaStream_t st);
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
                          const struct PeerView* pv, cudaStream_t st);
-// Peer mode: phases 1-3b in one cooperative launch when every row's CTA can be resident
-// and a row fits one CTA (N_local <= 32768); *launched tells whether it ran.
+// Peer mode: phases 1-3b in one cooperative launch when every rank's chunk fits one CTA
+// per row (n_local_max, the longest chunk of all ranks, <= 32768: every rank decides
+// alike); *launched tells whether it ran. DCR_ERR_SHAPE if the rows cannot all be
+// resident (every rank, same GPUs, fails alike).
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
-                              int k_eff, const struct PeerView* pv, cudaStream_t st,
-                              bool* launched);
+                              int n_local_max, int k_eff, const struct PeerView* pv,
+                              cudaStream_t st, bool* launched);
 
 // Projected-score mode (dcr_project.cu). Append: copies n_new rows of K and V into the
 // caches at position pos (k_cache may be null: no copy) and writes their projection

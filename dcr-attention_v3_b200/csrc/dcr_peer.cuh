@@ -139,4 +139,46 @@ __device__ __forceinline__ uint32_t ll_get(const PeerView& v, const uint64_t* p,
   return static_cast<uint32_t>(w);
 }
 
+// Packed histogram rows (the fused selection, whose counts fit 16 bits): word j carries
+// bins 3j, 3j+1, 3j+2 in bits 0-15, 16-31, 32-47 and a 16-bit tag of the step's epoch in
+// bits 48-63 (a slot is rewritten every step, so 16 bits tell this step's words from the
+// last step's; the tag is never 0, which a zeroed word carries). 86 words per row.
+constexpr int kPackedWords = (256 + 2) / 3;
+
+__device__ __forceinline__ uint32_t epoch_tag16(uint32_t epoch) { return epoch % 65535u + 1u; }
+
+__device__ __forceinline__ void ll_put_packed(uint64_t* p, uint32_t b0, uint32_t b1, uint32_t b2,
+                                              uint32_t epoch) {
+  const uint64_t w = (static_cast<uint64_t>(epoch_tag16(epoch)) << 48) |
+                     (static_cast<uint64_t>(b2 & 0xffffu) << 32) |
+                     (static_cast<uint64_t>(b1 & 0xffffu) << 16) | (b0 & 0xffffu);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// Waits (bounded, as ll_get) until the word at p carries `epoch` in its top 16 bits and
+// returns the word.
+__device__ __forceinline__ uint64_t ll_get_packed(const PeerView& v, const uint64_t* p,
+                                                  uint32_t epoch,
+                                                  uint64_t limit_ns = 2000000000ull) {
+  const uint32_t tag = epoch_tag16(epoch);
+  uint64_t w = ll_load(p);
+  if (static_cast<uint32_t>(w >> 48) == tag) return w;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    __nanosleep(32);
+    w = ll_load(p);
+    if (static_cast<uint32_t>(w >> 48) == tag) break;
+    if (((++spins) & 63u) == 0u) {
+      if (ld_volatile_u32(v.abort_word()) != 0u) break;
+      if (global_timer_ns() - t0 > limit_ns) {
+        raise_status(DCR_ERR_DEVICE_TIMEOUT);
+        atomicExch(v.abort_word(), 1u);
+        break;
+      }
+    }
+  }
+  return w;
+}
+
 }  // namespace dcr

@@ -92,8 +92,8 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
                                   int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                                   int64_t v_stride_h, int B, int H, int H_kv, int N_local, int D,
                                   int k_eff, float eps, void* const* peers, int world, int rank,
-                                  void* O, void* workspace, size_t workspace_bytes, void* stream,
-                                  void* const* events) {
+                                  int n_local_max, void* O, void* workspace,
+                                  size_t workspace_bytes, void* stream, void* const* events) {
   int st = check_heads(B, H, H_kv, N_local, D);
   if (st) return st;
   if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N_local))) return st;
@@ -101,6 +101,7 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
   if (Q == nullptr || O == nullptr || peers == nullptr) return DCR_ERR_NULL;
   if (!aligned16(Q) || !aligned16(O)) return DCR_ERR_ALIGN;
   if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world) return DCR_ERR_SHAPE;
+  if (n_local_max < N_local) return DCR_ERR_SHAPE;
   for (int p = 0; p < world; ++p)
     if (peers[p] == nullptr) return DCR_ERR_NULL;
   if (k_eff <= 0) return DCR_ERR_K_RANGE;
@@ -127,7 +128,8 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
     return st;
   if ((st = mark(1))) return st;
   bool fused = false;
-  if ((st = launch_shard_select_fused(w, ws, rows, N_local, k_eff, &v, s, &fused))) return st;
+  if ((st = launch_shard_select_fused(w, ws, rows, N_local, n_local_max, k_eff, &v, s, &fused)))
+    return st;
   if (fused) {
     if ((st = mark(2)) || (st = mark(3))) return st;
   } else {
@@ -159,25 +161,26 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
 int dcr_shard_decode_peer(const void* Q, const void* K, const void* V, int dtype,
                           int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                           int64_t v_stride_h, int B, int H, int H_kv, int N_local, int D,
-                          int k_eff, float eps, void* const* peers, int world, int rank, void* O,
-                          void* workspace, size_t workspace_bytes, void* stream) {
+                          int k_eff, float eps, void* const* peers, int world, int rank,
+                          int n_local_max, void* O, void* workspace, size_t workspace_bytes,
+                          void* stream) {
   return shard_decode_peer_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
-                                B, H, H_kv, N_local, D, k_eff, eps, peers, world, rank, O,
-                                workspace, workspace_bytes, stream, nullptr);
+                                B, H, H_kv, N_local, D, k_eff, eps, peers, world, rank,
+                                n_local_max, O, workspace, workspace_bytes, stream, nullptr);
 }
 
 int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int dtype,
                                 int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                                 int64_t v_stride_h, int B, int H, int H_kv, int N_local, int D,
                                 int k_eff, float eps, void* const* peers, int world, int rank,
-                                void* O, void* workspace, size_t workspace_bytes, void* stream,
-                                void* const* events) {
+                                int n_local_max, void* O, void* workspace,
+                                size_t workspace_bytes, void* stream, void* const* events) {
   if (events == nullptr) return DCR_ERR_NULL;
   for (int i = 0; i < 7; ++i)
     if (events[i] == nullptr) return DCR_ERR_NULL;
   return shard_decode_peer_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
-                                B, H, H_kv, N_local, D, k_eff, eps, peers, world, rank, O,
-                                workspace, workspace_bytes, stream, events);
+                                B, H, H_kv, N_local, D, k_eff, eps, peers, world, rank,
+                                n_local_max, O, workspace, workspace_bytes, stream, events);
 }
 
 }  // extern "C"

@@ -340,7 +340,8 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
 
 // Fused selection of the peer-exchange step (kernels above, phases 1-3b, in one launch):
 // one 512-thread CTA per row holds the row's keys in registers (up to 64 per thread)
-// through both histogram exchanges. The CTA publishes its row's high-byte histogram into
+// through both histogram exchanges, which use packed words (every rank's chunk is at
+// most 32768 positions, so counts fit 16 bits). The CTA publishes its row's high-byte histogram into
 // slot `rank` of every rank's buffer (exchange 0), reads every rank's row as its words
 // arrive, finds BH, publishes the low-byte histogram of its keys in BH (exchange 1),
 // reads, finds T and its tie quota, and emits its positions as Pass 2 does. Each row
@@ -348,6 +349,32 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
 // CTA resident) so that no row waits behind a CTA that cannot start.
 constexpr int kFsThreads = 512;
 constexpr int kFsWarps = kFsThreads / 32;
+
+// Publishes this row's 256-bin histogram h (exchange x, packed words) into slot `rank` of
+// every rank's buffer and sums every rank's row into out. Block-wide; ends with a barrier.
+__device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, int64_t row,
+                                                    const uint32_t* h, uint32_t* out,
+                                                    uint32_t epoch) {
+  const int tid = threadIdx.x;
+  if (tid < kPackedWords) {
+    const int b = 3 * tid;
+    const uint32_t c0 = h[b], c1 = b + 1 < 256 ? h[b + 1] : 0u, c2 = b + 2 < 256 ? h[b + 2] : 0u;
+    for (int q = 0; q < v.world; ++q)
+      ll_put_packed((x ? v.hl(q, v.rank, row) : v.hh(q, v.rank, row)) + tid, c0, c1, c2, epoch);
+    uint32_t s0 = 0, s1 = 0, s2 = 0;
+    for (int r = 0; r < v.world; ++r) {
+      const uint64_t w =
+          ll_get_packed(v, (x ? v.hl(v.rank, r, row) : v.hh(v.rank, r, row)) + tid, epoch);
+      s0 += static_cast<uint32_t>(w & 0xffffu);
+      s1 += static_cast<uint32_t>((w >> 16) & 0xffffu);
+      s2 += static_cast<uint32_t>((w >> 32) & 0xffffu);
+    }
+    out[b] = s0;
+    if (b + 1 < 256) out[b + 1] = s1;
+    if (b + 2 < 256) out[b + 2] = s2;
+  }
+  __syncthreads();
+}
 
 template <int VPT>
 __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const ShardParams p) {
@@ -393,14 +420,8 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
   for (int e = 0; e < kKeys; ++e)
     if (key[e] != 0u) atomicAdd(&hist[key[e] >> 8], 1u);
   __syncthreads();
-  if (tid < 256) {
-    const uint32_t c = hist[tid];
-    for (int q = 0; q < v.world; ++q) ll_put(v.hh(q, rank, row) + tid, c, epoch);  // own too
-    uint32_t sum = 0;
-    for (int r = 0; r < v.world; ++r) sum += ll_get(v, v.hh(rank, r, row) + tid, epoch);
-    hsum[tid] = sum;
-    hist[tid] = 0u;
-  }
+  exchange_row_packed(v, 0, row, hist, hsum, epoch);
+  if (tid < 256) hist[tid] = 0u;
   __syncthreads();
   if (warp == 0) {
     int bin;
@@ -426,13 +447,7 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
   for (int e = 0; e < kKeys; ++e)
     if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist[key[e] & 0xffu], 1u);
   __syncthreads();
-  if (tid < 256) {
-    const uint32_t c = hist[tid];
-    for (int q = 0; q < v.world; ++q) ll_put(v.hl(q, rank, row) + tid, c, epoch);
-    uint32_t sum = 0;
-    for (int r = 0; r < v.world; ++r) sum += ll_get(v, v.hl(rank, r, row) + tid, epoch);
-    hsum[tid] = sum;
-  }
+  exchange_row_packed(v, 1, row, hist, hsum, epoch);
   __syncthreads();
   if (warp == 0) {
     int bl;
@@ -447,7 +462,10 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
       const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
       const int need = p.k - static_cast<int>(s_above + above_lo);
       int eq_lower = 0;
-      for (int r = 0; r < rank; ++r) eq_lower += static_cast<int>(ll_get(v, v.hl(rank, r, row) + bl, epoch));
+      for (int r = 0; r < rank; ++r) {
+        const uint64_t w = ll_get_packed(v, v.hl(rank, r, row) + bl / 3, epoch);
+        eq_lower += static_cast<int>((w >> (16 * (bl % 3))) & 0xffffu);
+      }
       const int eq_mine = static_cast<int>(hist[bl]);
       s_T = T;
       s_quota = static_cast<uint32_t>(max(0, min(need - eq_lower, eq_mine)));
@@ -611,7 +629,7 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, shard_select_fused_kernel<VPT>,
                                                     kFsThreads, 0) != cudaSuccess)
     return DCR_ERR_CUDA;
-  if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_OK;  // not resident
+  if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_ERR_SHAPE;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.rows));
   cfg.blockDim = dim3(kFsThreads);
@@ -629,10 +647,12 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
 }
 
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
-                              int k_eff, const PeerView* pv, cudaStream_t st, bool* launched) {
+                              int n_local_max, int k_eff, const PeerView* pv, cudaStream_t st,
+                              bool* launched) {
   *launched = false;
+  // every rank takes the same path: decided from the longest chunk of all ranks
+  if (pv == nullptr || n_local_max > kFsThreads * 64 || N_local > n_local_max) return DCR_OK;
   const int nvec = (N_local + 7) / 8;
-  if (pv == nullptr || nvec > kFsThreads * 8) return DCR_OK;
   ShardParams p = shard_params(w, ws, rows, N_local, k_eff);
   p.v = *pv;
   p.world = pv->world;

@@ -83,11 +83,11 @@ SIGNATURES = {
     "dcr_xchg_reset": (_i32, [_vp, _i32, _i32, _i32, _vp]),
     "dcr_shard_decode_peer": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32,
                                      _i32, _i32, _i32, _i32, _f32, ctypes.POINTER(_vp), _i32,
-                                     _i32, _vp, _vp, _sz, _vp]),
+                                     _i32, _i32, _vp, _vp, _sz, _vp]),
     "dcr_shard_decode_peer_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32,
                                            _i32, _i32, _i32, _i32, _i32, _f32,
-                                           ctypes.POINTER(_vp), _i32, _i32, _vp, _vp, _sz, _vp,
-                                           ctypes.POINTER(_vp)]),
+                                           ctypes.POINTER(_vp), _i32, _i32, _i32, _vp, _vp, _sz,
+                                           _vp, ctypes.POINTER(_vp)]),
     "dcr_read_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
 }
 

@@ -293,8 +293,8 @@ class SequenceShardedDecoder:
             code = st.lib.dcr_shard_decode_peer(
                 st.Q.data_ptr(), st.K.data_ptr(), st.V.data_ptr(), st.dt, st.ksb, st.ksh,
                 st.vsb, st.vsh, st.B, st.H, st.H_kv, st.N, HEAD_DIM, st.k, st.eps,
-                self.peer.peers, self.peer.world, self.peer.rank, out.data_ptr(),
-                st.ws.data_ptr(), st.ws_bytes, st._stream())
+                self.peer.peers, self.peer.world, self.peer.rank, max(self.n_locals),
+                out.data_ptr(), st.ws.data_ptr(), st.ws_bytes, st._stream())
             _lib.check(code, "dcr_shard_decode_peer")
             return out
 

@@ -291,12 +291,15 @@ int dcr_xchg_destroy(void* buf);
 int dcr_xchg_reset(void* buf, int B, int H, int world, void* stream);
 
 /* One sequence-sharded decode step of this rank (arguments as dcr_shard_attend, with the
- * workspace of dcr_shard_workspace_bytes); returns O [B, H, D] on every rank. */
+ * workspace of dcr_shard_workspace_bytes); returns O [B, H, D] on every rank.
+ * n_local_max is the longest N_local of all ranks (the same value on every rank, and
+ * constant for one exchange buffer: reset the buffers on every rank after changing it);
+ * it selects the step's kernels and exchange format alike on every rank. */
 int dcr_shard_decode_peer(const void* Q, const void* K, const void* V, int dtype,
                           int64_t k_stride_b, int64_t k_stride_h,
                           int64_t v_stride_b, int64_t v_stride_h,
                           int B, int H, int H_kv, int N_local, int D, int k_eff, float eps,
-                          void* const* peers, int world, int rank, void* O,
+                          void* const* peers, int world, int rank, int n_local_max, void* O,
                           void* workspace, size_t workspace_bytes, void* stream);
 
 /* dcr_shard_decode_peer with seven caller-created CUDA events recorded on the stream
@@ -306,9 +309,9 @@ int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int
                                 int64_t k_stride_b, int64_t k_stride_h,
                                 int64_t v_stride_b, int64_t v_stride_h,
                                 int B, int H, int H_kv, int N_local, int D, int k_eff,
-                                float eps, void* const* peers, int world, int rank, void* O,
-                                void* workspace, size_t workspace_bytes, void* stream,
-                                void* const* events);
+                                float eps, void* const* peers, int world, int rank,
+                                int n_local_max, void* O, void* workspace,
+                                size_t workspace_bytes, void* stream, void* const* events);
 
 /* Synchronises the current device and returns (in *status_out) the OR of the device
  * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.

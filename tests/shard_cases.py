@@ -28,6 +28,8 @@ CASES = {
     "gqa8_f32_4r": (1, 8, 1, [512, 512, 512, 512], 308, "f32", "plain"),
     "empty_rank_2r": (1, 1, 1, [400, 200], 100, "bf16", "empty_rank"),
     "gqa2_bf16_2r": (2, 4, 2, [1031, 997], 0.3, "bf16", "plain"),
+    # a chunk longer than one CTA's 32768 keys: the peer step's accumulating phase kernels
+    "long_2r": (1, 4, 1, [40000, 30008], 0.05, "bf16", "plain"),
 }
 
 CASES_BY_WORLD = {}

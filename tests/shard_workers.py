@@ -73,7 +73,8 @@ def gloo_rank(rank: int, world: int, port: int, out_dir: str) -> None:
 def nccl_cases():
     """(name, (Q, K, V, splits, k)) of the 2-GPU test, on the CPU."""
     from shard_cases import make_case
-    return [(n, make_case(n)) for n in ("bf16_2r", "ties_2r", "empty_rank_2r", "gqa2_bf16_2r")]
+    return [(n, make_case(n)) for n in ("bf16_2r", "ties_2r", "empty_rank_2r", "gqa2_bf16_2r",
+                                        "long_2r")]
 
 
 def nccl_rank(rank: int, world: int, port: int, out_dir: str) -> None:

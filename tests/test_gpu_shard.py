@@ -236,8 +236,8 @@ def test_peer_wait_expires_and_reports(cuda_lib):
     t0 = time.perf_counter()
     st = lib.dcr_shard_decode_peer(Q.data_ptr(), K.data_ptr(), V.data_ptr(), 0, step.ksb,
                                    step.ksh, step.vsb, step.vsh, B, H, H_kv, N, 64, k, 1e-12,
-                                   peers, 2, 0, O.data_ptr(), step.ws.data_ptr(), step.ws_bytes,
-                                   None)
+                                   peers, 2, 0, N, O.data_ptr(), step.ws.data_ptr(),
+                                   step.ws_bytes, None)
     assert st == 0
     status = _lib.read_device_status(clear=True)       # synchronises
     elapsed = time.perf_counter() - t0
@@ -252,7 +252,7 @@ def test_peer_wait_expires_and_reports(cuda_lib):
     peers1 = (ctypes.c_void_p * 1)(one.value)
     st = lib.dcr_shard_decode_peer(Q.data_ptr(), K.data_ptr(), V.data_ptr(), 0, step.ksb,
                                    step.ksh, step.vsb, step.vsh, B, H, H_kv, N, 64, k, 1e-12,
-                                   peers1, 1, 0, O.data_ptr(), step.ws.data_ptr(),
+                                   peers1, 1, 0, N, O.data_ptr(), step.ws.data_ptr(),
                                    step.ws_bytes, None)
     assert st == 0
     assert _lib.read_device_status(clear=True) == 0
