@@ -546,11 +546,15 @@ def run_sharded_arm(args):
         n_local, h_kv_local = CFG["N"], H_kv // world
         N = n_local
     k = _k_eff(N, CFG["coverage"])
+    # each layer is one sequence: its outlier channels are shared by every rank's chunk and
+    # its sinks are positions 0-3 (rank 0's chunk in the sequence split)
+    from dcr_b200.synthetic import outlier_channels
     caches = []
     for L in range(LAYERS):
         g = torch.Generator(device=dev).manual_seed(1000 * rank + L)
         _, K, V = make_decode_inputs(B, H, h_kv_local, n_local, dtype=dt, device=dev,
-                                     generator=g)
+                                     generator=g, channels=outlier_channels(seed=L, device=dev),
+                                     sink_rows=4 if (rank == 0 or not seq) else 0)
         caches.append((K, V))
     Qs = fresh_queries(max(steps, warm) + 1, B, H, dtype=dt, seed=7, device=dev)  # replicated
     O = torch.empty(B, H, D, dtype=dt, device=dev)

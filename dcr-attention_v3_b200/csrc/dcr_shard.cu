@@ -106,8 +106,13 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   if (kLevel == 1) {
     const uint32_t* hist_hi = reinterpret_cast<const uint32_t*>(p.hist_hi + row * 256);
     if (peer) {
+      uint64_t w[kMaxPeers];
+      ll_gather(p.v, p.v.hh(p.v.rank, 0, row) + tid, static_cast<int64_t>(p.v.rows) * 256, epoch,
+                32, w);
       uint32_t sum = 0;
-      for (int r = 0; r < p.v.world; ++r) sum += ll_get(p.v, p.v.hh(p.v.rank, r, row) + tid, epoch);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < p.v.world) sum += static_cast<uint32_t>(w[r]);
       hsum[tid] = sum;
       __syncthreads();
       hist_hi = hsum;
@@ -185,7 +190,16 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
         __ldcg(p.hist_lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + b));
   };
   uint32_t tot = 0;
-  for (int r = 0; r < p.world; ++r) tot += lo(r, tid);
+  if (peer) {
+    uint64_t w[kMaxPeers];
+    ll_gather(p.v, p.v.hl(p.v.rank, 0, row) + tid, static_cast<int64_t>(p.v.rows) * 256, epoch,
+              32, w);
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < p.v.world) tot += static_cast<uint32_t>(w[r]);
+  } else {
+    for (int r = 0; r < p.world; ++r) tot += lo(r, tid);
+  }
   h[tid] = tot;
   uint32_t key[kShKeys];
   shard_load_keys(p, row, chunk, key);
@@ -313,19 +327,36 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
   const int64_t row = blockIdx.x;
   const int tid = threadIdx.x;
   const uint32_t epoch = v.world > 0 ? step_epoch(v) : 0u;
-  // word i of rank r's state of this row
-  auto state = [&](int r, int i) -> float {
-    if (v.world > 0) return __uint_as_float(ll_get(v, v.st(v.rank, r, row) + i, epoch));
-    return __ldcg(states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats + i);
-  };
-  float M = -INFINITY;
-  for (int r = 0; r < world; ++r) M = fmaxf(M, state(r, 0));
-  float L = 0.0f, o = 0.0f;
-  for (int r = 0; r < world; ++r) {
-    const float m = state(r, 0);
-    const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
-    L = fmaf(w, state(r, 1), L);
-    o = fmaf(w, state(r, 2 + tid), o);
+  float M = -INFINITY, L = 0.0f, o = 0.0f;
+  if (v.world > 0) {
+    // every rank's (m, l, o[tid]) of this row, each gathered in one round trip
+    uint64_t wm[kMaxPeers], wl[kMaxPeers], wo[kMaxPeers];
+    const int64_t stride = static_cast<int64_t>(v.rows) * kShStateFloats;
+    const uint64_t* base = v.st(v.rank, 0, row);
+    ll_gather(v, base, stride, epoch, 32, wm);
+    ll_gather(v, base + 1, stride, epoch, 32, wl);
+    ll_gather(v, base + 2 + tid, stride, epoch, 32, wo);
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r)
+      if (r < v.world) M = fmaxf(M, __uint_as_float(static_cast<uint32_t>(wm[r])));
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r >= v.world) break;
+      const float m = __uint_as_float(static_cast<uint32_t>(wm[r]));
+      const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+      L = fmaf(w, __uint_as_float(static_cast<uint32_t>(wl[r])), L);
+      o = fmaf(w, __uint_as_float(static_cast<uint32_t>(wo[r])), o);
+    }
+  } else {
+    for (int r = 0; r < world; ++r)
+      M = fmaxf(M, __ldcg(states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats));
+    for (int r = 0; r < world; ++r) {
+      const float* st = states + (static_cast<int64_t>(r) * rows + row) * kShStateFloats;
+      const float m = __ldcg(st);
+      const float w = (m == -INFINITY) ? 0.0f : exp2f(m - M);
+      L = fmaf(w, __ldcg(st + 1), L);
+      o = fmaf(w, __ldcg(st + 2 + tid), o);
+    }
   }
   ElemTraits<T>::store(O, static_cast<int>(row * kD + tid), o / L);
   if (v.world > 0) {
@@ -345,8 +376,9 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
 // slot `rank` of every rank's buffer (exchange 0), reads every rank's row as its words
 // arrive, finds BH, publishes the low-byte histogram of its keys in BH (exchange 1),
 // reads, finds T and its tie quota, and emits its positions as Pass 2 does. Each row
-// waits only for the same row of the other ranks; the launch is cooperative (every row's
-// CTA resident) so that no row waits behind a CTA that cannot start.
+// waits only for the same row of the other ranks, never for another CTA of its own GPU;
+// the kernel runs only when all its rows fit in one wave (every rank alike), so no row
+// waits behind a row that the other GPU has not started.
 constexpr int kFsThreads = 512;
 constexpr int kFsWarps = kFsThreads / 32;
 
@@ -361,13 +393,16 @@ __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, in
     const uint32_t c0 = h[b], c1 = b + 1 < 256 ? h[b + 1] : 0u, c2 = b + 2 < 256 ? h[b + 2] : 0u;
     for (int q = 0; q < v.world; ++q)
       ll_put_packed((x ? v.hl(q, v.rank, row) : v.hh(q, v.rank, row)) + tid, c0, c1, c2, epoch);
+    uint64_t w[kMaxPeers];
+    ll_gather(v, (x ? v.hl(v.rank, 0, row) : v.hh(v.rank, 0, row)) + tid,
+              static_cast<int64_t>(v.rows) * 256, epoch, 48, w);
     uint32_t s0 = 0, s1 = 0, s2 = 0;
-    for (int r = 0; r < v.world; ++r) {
-      const uint64_t w =
-          ll_get_packed(v, (x ? v.hl(v.rank, r, row) : v.hh(v.rank, r, row)) + tid, epoch);
-      s0 += static_cast<uint32_t>(w & 0xffffu);
-      s1 += static_cast<uint32_t>((w >> 16) & 0xffffu);
-      s2 += static_cast<uint32_t>((w >> 32) & 0xffffu);
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r >= v.world) break;
+      s0 += static_cast<uint32_t>(w[r] & 0xffffu);
+      s1 += static_cast<uint32_t>((w[r] >> 16) & 0xffffu);
+      s2 += static_cast<uint32_t>((w[r] >> 32) & 0xffffu);
     }
     out[b] = s0;
     if (b + 1 < 256) out[b + 1] = s1;
@@ -635,11 +670,8 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
   cfg.blockDim = dim3(kFsThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
   if (cudaLaunchKernelEx(&cfg, shard_select_fused_kernel<VPT>, p) != cudaSuccess)
     return DCR_ERR_CUDA;
   *launched = true;
