@@ -383,15 +383,15 @@ def run_gpu_arm(args):
         K, V = caches[i % LAYERS]
         st = lib.dcr_decode_projected(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), V.data_ptr(),
                                       kps[i % LAYERS].data_ptr(), dcode, ksb, ksh, ksb, ksh,
-                                      kpsb, kpsh, Pd.data_ptr(), 16, B, H, H_kv, N, D, k, 1e-12,
-                                      O.data_ptr(), ws.data_ptr(), ws_n, sptr)
+                                      kpsb, kpsh, Pd.data_ptr(), 16, None, B, H, H_kv, N, D, k,
+                                      1e-12, O.data_ptr(), ws.data_ptr(), ws_n, sptr)
         if st:
             raise _lib.DCRError(st, "dcr_decode_projected")
 
     def pass1_proj(i, sptr):
         st = lib.dcr_score_projected(kps[i % LAYERS].data_ptr(), dcode, kpsb, kpsh,
-                                     Qs[i % Qs.shape[0]].data_ptr(), 1e-12, Pd.data_ptr(), 16, B,
-                                     H, H_kv, N, D, sc_buf.data_ptr(), N, sptr)
+                                     Qs[i % Qs.shape[0]].data_ptr(), 1e-12, Pd.data_ptr(), 16,
+                                     None, B, H, H_kv, N, D, sc_buf.data_ptr(), N, sptr)
         if st:
             raise _lib.DCRError(st, "dcr_score_projected")
 

@@ -6,6 +6,7 @@
 #include "dcr_attend.cu"
 #include "dcr_shard.cu"
 #include "dcr_project.cu"
+#include "dcr_rope.cu"
 #include "dcr_capi.cu"
 #include "dcr_peer_capi.cu"
 #include "dcr_noalloc.cu"

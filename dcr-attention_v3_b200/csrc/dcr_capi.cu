@@ -250,6 +250,7 @@ struct ProjArgs {
   const void* kp;
   int64_t psb, psh;
   const float* P;
+  const float* qp;  // optional projected unit queries
 };
 
 static int check_proj(const void* KP, int dtype, int64_t& psb, int64_t& psh, int B, int H_kv,
@@ -299,8 +300,8 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   if ((st = mark(0))) return st;
   // Pass 1 stores order keys, which Pass 2 reads directly.
   if (proj != nullptr)
-    st = launch_score_projected(proj->kp, dtype, proj->psb, proj->psh, Q, proj->P, eps, B, H,
-                                H_kv, N, scores, w.n_pad, 1, s);
+    st = launch_score_projected(proj->kp, dtype, proj->psb, proj->psh, Q, proj->P, proj->qp,
+                                eps, B, H, H_kv, N, scores, w.n_pad, 1, s);
   else
     st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
                       w.n_pad, 1, s);
@@ -370,22 +371,24 @@ int dcr_cache_append(const void* K_new, const void* V_new, int dtype, int64_t ne
 }
 
 int dcr_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
-                        const void* Q, float eps, const float* P, int R, int B, int H, int H_kv,
-                        int N, int D, uint16_t* scores, int64_t s_stride_row, void* stream) {
+                        const void* Q, float eps, const float* P, int R, const float* qp, int B,
+                        int H, int H_kv, int N, int D, uint16_t* scores, int64_t s_stride_row,
+                        void* stream) {
   int st = check_heads(B, H, H_kv, N, D);
   if (st) return st;
   if ((st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R))) return st;
   if (Q == nullptr || scores == nullptr) return DCR_ERR_NULL;
   if (!aligned16(Q)) return DCR_ERR_ALIGN;
   if (s_stride_row < N) return DCR_ERR_SHAPE;
-  return launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, eps, B, H, H_kv, N,
-                                scores, s_stride_row, 0, static_cast<cudaStream_t>(stream));
+  return launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, qp, eps, B, H, H_kv,
+                                N, scores, s_stride_row, 0, static_cast<cudaStream_t>(stream));
 }
 
 int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64_t p_stride_b,
-                                 int64_t p_stride_h, const float* P, int R, int B, int H,
-                                 int H_kv, int N, int D, int k_eff, float eps, int32_t* idx_out,
-                                 void* workspace, size_t workspace_bytes, void* stream) {
+                                 int64_t p_stride_h, const float* P, int R, const float* qp,
+                                 int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                                 int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                                 void* stream) {
   int st = check_heads(B, H, H_kv, N, D);
   if (st) return st;
   if ((st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R))) return st;
@@ -398,8 +401,8 @@ int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64
   if (!aligned16(workspace)) return DCR_ERR_ALIGN;
   uint16_t* scores = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + w.scores);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if ((st = launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, eps, B, H, H_kv, N,
-                                   scores, w.n_pad, 1, s)))
+  if ((st = launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, qp, eps, B, H,
+                                   H_kv, N, scores, w.n_pad, 1, s)))
     return st;
   return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
 }
@@ -407,15 +410,42 @@ int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64
 int dcr_decode_projected(const void* Q, const void* K, const void* V, const void* KP, int dtype,
                          int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                          int64_t v_stride_h, int64_t p_stride_b, int64_t p_stride_h,
-                         const float* P, int R, int B, int H, int H_kv, int N, int D, int k_eff,
-                         float eps, void* O, void* workspace, size_t workspace_bytes,
-                         void* stream) {
+                         const float* P, int R, const float* qp, int B, int H, int H_kv, int N,
+                         int D, int k_eff, float eps, void* O, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   if (B <= 0 || H_kv <= 0 || N <= 0) return DCR_ERR_SHAPE;
   const int st = check_proj(KP, dtype, p_stride_b, p_stride_h, B, H_kv, N, P, R);
   if (st) return st;
-  const ProjArgs proj = {KP, p_stride_b, p_stride_h, P};
+  const ProjArgs proj = {KP, p_stride_b, p_stride_h, P, qp};
   return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
                      N, D, k_eff, eps, O, workspace, workspace_bytes, stream, nullptr, &proj);
+}
+
+int dcr_decode_prologue(const void* q, const void* k, const void* v, const void* cos,
+                        const void* sin, int dtype, int B, int H, int H_kv, int D, void* q_out,
+                        void* K_cache, void* V_cache, int64_t c_stride_b, int64_t c_stride_h,
+                        int pos, int N_max, const float* P, int R, void* KP_cache,
+                        int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
+                        void* stream) {
+  if (B <= 0 || H <= 0 || H_kv <= 0 || N_max <= 0 || D != kD || H % H_kv != 0)
+    return DCR_ERR_SHAPE;
+  if (pos < 0 || pos >= N_max) return DCR_ERR_SHAPE;
+  if (q == nullptr || k == nullptr || v == nullptr || cos == nullptr || sin == nullptr ||
+      q_out == nullptr)
+    return DCR_ERR_NULL;
+  if (dtype_bytes(dtype) == 0) return DCR_ERR_DTYPE;
+  int64_t cvb = c_stride_b, cvh = c_stride_h;
+  int st = check_cache(K_cache, dtype, c_stride_b, c_stride_h, B, H_kv, N_max);
+  if (st) return st;
+  if ((st = check_cache(V_cache, dtype, cvb, cvh, B, H_kv, N_max))) return st;
+  if ((KP_cache != nullptr || qp_out != nullptr) && (P == nullptr || R != DCR_PROJ_RANK))
+    return P == nullptr ? DCR_ERR_NULL : DCR_ERR_SHAPE;
+  if (KP_cache != nullptr &&
+      (st = check_proj(KP_cache, dtype, p_stride_b, p_stride_h, B, H_kv, N_max, P, R)))
+    return st;
+  return launch_rope_append(q, k, v, cos, sin, dtype, B, H, H_kv, q_out, K_cache, V_cache,
+                            c_stride_b, c_stride_h, pos, KP_cache, p_stride_b, p_stride_h, P,
+                            qp_out, eps, static_cast<cudaStream_t>(stream));
 }
 
 // ---- sequence-sharded decode ----------------------------------------------------------

@@ -117,9 +117,17 @@ int launch_append(const void* k_new, const void* v_new, int64_t nsb, int64_t nsh
                   void* v_cache, int64_t csb, int64_t csh, void* kp, int64_t psb, int64_t psh,
                   const float* P, int B, int H_kv, int n_new, int pos, int dtype,
                   cudaStream_t st);
+// qp (optional): the projected unit queries [B*H][R] (from the decode prologue).
 int launch_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
-                           const void* Q, const float* P, float eps, int B, int H, int H_kv,
-                           int N, uint16_t* scores, int64_t s_stride, int keys_out,
-                           cudaStream_t st);
+                           const void* Q, const float* P, const float* qp, float eps, int B,
+                           int H, int H_kv, int N, uint16_t* scores, int64_t s_stride,
+                           int keys_out, cudaStream_t st);
+// Decode prologue (dcr_rope.cu): RoPE of the step's q and k rows, cache append at pos,
+// and (optional) KP of the new key row and the projected unit queries qp.
+int launch_rope_append(const void* q, const void* k, const void* v, const void* cos,
+                       const void* sin, int dtype, int B, int H, int H_kv, void* q_out,
+                       void* k_cache, void* v_cache, int64_t csb, int64_t csh, int pos,
+                       void* kp, int64_t psb, int64_t psh, const float* P, float* qp,
+                       float eps, cudaStream_t st);
 
 }  // namespace dcr

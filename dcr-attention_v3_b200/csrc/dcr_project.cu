@@ -108,6 +108,7 @@ struct ProjScoreParams {
   int64_t psb, psh;
   const void* q;       // [B, H, D]
   const float* P;      // [D][R]
+  const float* qp;     // optional [B*H][R]: the projected unit queries (else computed here)
   float eps;
   int H_kv, N, tiles;  // tiles = ceil(N / kSpRows) per (b, h_kv)
   int cpg;             // CTAs per (b, h_kv): CTA c of a group takes tiles c, c + cpg, ...
@@ -144,17 +145,23 @@ __global__ void __launch_bounds__(kSpThreads) score_proj_kernel(const ProjScoreP
 
   // unit queries of the G heads (one warp each; unit_query_warp of dcr_score.cu, the same
   // arithmetic as Pass 1), then their projections
-  for (int h = warp; h < G; h += kSpThreads / 32) {
-    const char* q_row = static_cast<const char*>(p.q) + (static_cast<size_t>(g) * G + h) * kD * sizeof(T);
-    unit_query_warp<T>(q_row, p.eps, &u_s[h][0]);
-  }
-  __syncthreads();
-  for (int i = tid; i < G * kProjR; i += kSpThreads) {
-    const int h = i / kProjR, jj = i % kProjR;
-    float acc = 0.0f;
+  if (p.qp != nullptr) {
+    for (int i = tid; i < G * kProjR; i += kSpThreads)
+      qp_s[i / kProjR][i % kProjR] = __ldg(p.qp + static_cast<int64_t>(g) * G * kProjR + i);
+  } else {
+    for (int h = warp; h < G; h += kSpThreads / 32) {
+      const char* q_row =
+          static_cast<const char*>(p.q) + (static_cast<size_t>(g) * G + h) * kD * sizeof(T);
+      unit_query_warp<T>(q_row, p.eps, &u_s[h][0]);
+    }
+    __syncthreads();
+    for (int i = tid; i < G * kProjR; i += kSpThreads) {
+      const int h = i / kProjR, jj = i % kProjR;
+      float acc = 0.0f;
 #pragma unroll 16
-    for (int d = 0; d < kD; ++d) acc = fmaf(u_s[h][d], __ldg(p.P + d * kProjR + jj), acc);
-    qp_s[h][jj] = acc;
+      for (int d = 0; d < kD; ++d) acc = fmaf(u_s[h][d], __ldg(p.P + d * kProjR + jj), acc);
+      qp_s[h][jj] = acc;
+    }
   }
   __syncthreads();
   float2 qp[G][kProjR / 2];
@@ -275,10 +282,11 @@ static int launch_score_proj_t(ProjScoreParams p, int B, int G, cudaStream_t st)
 }
 
 int launch_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
-                           const void* Q, const float* P, float eps, int B, int H, int H_kv,
-                           int N, uint16_t* scores, int64_t s_stride, int keys_out,
-                           cudaStream_t st) {
+                           const void* Q, const float* P, const float* qp, float eps, int B,
+                           int H, int H_kv, int N, uint16_t* scores, int64_t s_stride,
+                           int keys_out, cudaStream_t st) {
   ProjScoreParams p;
+  p.qp = qp;
   p.kp = KP;
   p.psb = p_stride_b;
   p.psh = p_stride_h;

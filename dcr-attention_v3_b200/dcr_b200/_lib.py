@@ -59,13 +59,17 @@ SIGNATURES = {
                                 _i64, _i64, _vp]),
     "dcr_cache_append": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp,
                                 _i64, _i64, _i32, _i32, _vp, _i32, _vp, _i64, _i64, _vp]),
-    "dcr_score_projected": (_i32, [_vp, _i32, _i64, _i64, _vp, _f32, _vp, _i32, _i32, _i32,
-                                   _i32, _i32, _i32, _vp, _i64, _vp]),
-    "dcr_select_indices_projected": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _i32, _i32,
-                                            _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp]),
+    "dcr_score_projected": (_i32, [_vp, _i32, _i64, _i64, _vp, _f32, _vp, _i32, _vp, _i32,
+                                   _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
+    "dcr_select_indices_projected": (_i32, [_vp, _vp, _i32, _i64, _i64, _vp, _i32, _vp, _i32,
+                                            _i32, _i32, _i32, _i32, _i32, _f32, _vp, _vp, _sz,
+                                            _vp]),
     "dcr_decode_projected": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64,
-                                    _i64, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _f32,
-                                    _vp, _vp, _sz, _vp]),
+                                    _i64, _vp, _i32, _vp, _i32, _i32, _i32, _i32, _i32, _i32,
+                                    _f32, _vp, _vp, _sz, _vp]),
+    "dcr_decode_prologue": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
+                                   _vp, _vp, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _i64, _i64,
+                                   _vp, _f32, _vp]),
     "dcr_shard_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "dcr_shard_score": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,
                                _f32, _vp, _vp, _sz, _vp]),

@@ -86,8 +86,8 @@ def topk_qaxis_select_projected(Q: torch.Tensor, KP_cache: torch.Tensor, P: torc
     ws = workspace(Q.device, workspace_bytes(B, H, H_kv, N, k_eff), workspace_buf)
     with torch.cuda.device(Q.device):
         st = _lib.load().dcr_select_indices_projected(
-            Q.data_ptr(), KP_cache.data_ptr(), dt, psb, psh, P.data_ptr(), PROJ_RANK, B, H, H_kv,
-            N, HEAD_DIM, int(k_eff), float(eps), idx.data_ptr(), ws.data_ptr(), ws.numel(),
+            Q.data_ptr(), KP_cache.data_ptr(), dt, psb, psh, P.data_ptr(), PROJ_RANK, None, B, H,
+            H_kv, N, HEAD_DIM, int(k_eff), float(eps), idx.data_ptr(), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(Q.device))
     _lib.check(st, "dcr_select_indices_projected")
     return idx
@@ -97,8 +97,10 @@ def topk_qaxis_attention_projected(Q: torch.Tensor, K_cache: torch.Tensor,
                                    V_cache: torch.Tensor, KP_cache: torch.Tensor,
                                    P: torch.Tensor, k_eff: int, *, eps: float = 1e-12,
                                    out: Optional[torch.Tensor] = None,
-                                   workspace_buf: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Decode step with the projected Pass 1: O [B, H, D] in Q's dtype."""
+                                   workspace_buf: Optional[torch.Tensor] = None,
+                                   qp: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Decode step with the projected Pass 1: O [B, H, D] in Q's dtype. ``qp`` (optional):
+    the projected unit queries [B, H, 16] fp32 from :func:`decode_prologue`."""
     B, H, H_kv, N, dt, psb, psh = _check_q_kp(Q, KP_cache, P)
     _lib.require_cuda(K_cache, V_cache)
     require(tuple(K_cache.shape) == (B, H_kv, N, HEAD_DIM) and
@@ -115,9 +117,14 @@ def topk_qaxis_attention_projected(Q: torch.Tensor, K_cache: torch.Tensor,
                 "out must be a contiguous [B, H, D] tensor like Q")
     ws = workspace(Q.device, workspace_bytes(B, H, H_kv, N, k_eff), workspace_buf)
     with torch.cuda.device(Q.device):
+        qp_ptr = None
+        if qp is not None:
+            require(qp.dtype == torch.float32 and qp.is_contiguous() and
+                    tuple(qp.shape) == (B, H, PROJ_RANK), "qp must be a contiguous fp32 [B, H, 16]")
+            qp_ptr = qp.data_ptr()
         st = _lib.load().dcr_decode_projected(
             Q.data_ptr(), K_cache.data_ptr(), V_cache.data_ptr(), KP_cache.data_ptr(), dt, ksb,
-            ksh, vsb, vsh, psb, psh, P.data_ptr(), PROJ_RANK, B, H, H_kv, N, HEAD_DIM,
+            ksh, vsb, vsh, psb, psh, P.data_ptr(), PROJ_RANK, qp_ptr, B, H, H_kv, N, HEAD_DIM,
             int(k_eff), float(eps), out.data_ptr(), ws.data_ptr(), ws.numel(),
             _lib.stream_ptr(Q.device))
     _lib.check(st, "dcr_decode_projected")

@@ -12,7 +12,7 @@ without a copy.
 """
 from __future__ import annotations
 
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -80,3 +80,46 @@ class StaticKVCache:
                 _lib.stream_ptr(self.device))
         _lib.check(st, "dcr_cache_append")
         self.length += n_new
+
+    def append_rotated(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       cos: torch.Tensor, sin: torch.Tensor, *, want_qp: bool = False,
+                       eps: float = 1e-12) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+        """The decode prologue of one step in one launch (dcr_decode_prologue): RoPE of the
+        step's q [B, H, D] and k [B, H_kv, D] rows with the position embeddings cos, sin
+        [B, D] (HF apply_rotary_pos_emb, dcr_attention/models/llama/compat.py:63), the
+        rotated k and v appended at position ``length`` (with their projection when the
+        cache keeps KP). Returns (rotated q [B, H, D], projected unit queries [B, H, 16]
+        fp32 when ``want_qp`` and the cache has P, else None)."""
+        _lib.require_cuda(q, k, v, cos, sin)
+        B, H, D = q.shape
+        require(D == HEAD_DIM and B == self.B and tuple(k.shape) == (B, self.H_kv, D) and
+                tuple(v.shape) == (B, self.H_kv, D), "q [B, H, D], k and v [B, H_kv, D]")
+        require(all(t.dtype == self.dtype for t in (q, k, v, cos, sin)),
+                f"q, k, v, cos, sin must be {self.dtype}")
+        require(tuple(cos.shape) == (B, D) and tuple(sin.shape) == (B, D), "cos, sin [B, D]")
+        require(self.length < self.N_max, f"cache full: N_max={self.N_max}")
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        cos, sin = cos.contiguous(), sin.contiguous()
+        q_out = torch.empty_like(q)
+        qp = None
+        if want_qp:
+            require(self.P is not None, "want_qp needs a cache with a projection P")
+            qp = torch.empty(B, H, PROJ_RANK, dtype=torch.float32, device=self.device)
+        csb, csh = cache_strides(self.k, "K_cache")
+        if self.kp is not None:
+            psb, psh = kp_strides(self.kp)
+            kp_ptr = self.kp.data_ptr()
+        else:
+            psb = psh = 0
+            kp_ptr = None
+        P_ptr = self.P.data_ptr() if self.P is not None else None
+        with torch.cuda.device(self.device):
+            st = _lib.load().dcr_decode_prologue(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                _lib.DTYPE_CODES[self.dtype], B, H, self.H_kv, HEAD_DIM, q_out.data_ptr(),
+                self.k.data_ptr(), self.v.data_ptr(), csb, csh, self.length, self.N_max, P_ptr,
+                PROJ_RANK, kp_ptr, psb, psh, None if qp is None else qp.data_ptr(), float(eps),
+                _lib.stream_ptr(self.device))
+        _lib.check(st, "dcr_decode_prologue")
+        self.length += 1
+        return q_out, qp

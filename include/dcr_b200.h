@@ -189,26 +189,45 @@ int dcr_cache_append(const void* K_new, const void* V_new, int dtype,
                      int64_t c_stride_h, int pos, int N_max, const float* P, int R,
                      void* KP_cache, int64_t p_stride_b, int64_t p_stride_h, void* stream);
 
-/* Pass 1 of the projected mode: bf16 score bits [B*H, N] (row stride s_stride_row). */
+/* Pass 1 of the projected mode: bf16 score bits [B*H, N] (row stride s_stride_row).
+ * qp (optional, else NULL): the projected unit queries [B*H][R] fp32 that
+ * dcr_decode_prologue wrote; without it Pass 1 computes them from Q and P. */
 int dcr_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,
-                        const void* Q, float eps, const float* P, int R, int B, int H,
-                        int H_kv, int N, int D, uint16_t* scores, int64_t s_stride_row,
-                        void* stream);
+                        const void* Q, float eps, const float* P, int R, const float* qp,
+                        int B, int H, int H_kv, int N, int D, uint16_t* scores,
+                        int64_t s_stride_row, void* stream);
 
 /* Pass 1 (projected) + Pass 2: indices [B*H, k_eff] int32 ascending. Workspace as
  * dcr_workspace_bytes. */
 int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64_t p_stride_b,
-                                 int64_t p_stride_h, const float* P, int R, int B, int H,
-                                 int H_kv, int N, int D, int k_eff, float eps, int32_t* idx_out,
-                                 void* workspace, size_t workspace_bytes, void* stream);
+                                 int64_t p_stride_h, const float* P, int R, const float* qp,
+                                 int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                                 int32_t* idx_out, void* workspace, size_t workspace_bytes,
+                                 void* stream);
 
 /* Full decode step with projected Pass 1: O [B, H, D]. Workspace as dcr_workspace_bytes. */
 int dcr_decode_projected(const void* Q, const void* K, const void* V, const void* KP, int dtype,
                          int64_t k_stride_b, int64_t k_stride_h,
                          int64_t v_stride_b, int64_t v_stride_h,
                          int64_t p_stride_b, int64_t p_stride_h, const float* P, int R,
-                         int B, int H, int H_kv, int N, int D, int k_eff, float eps, void* O,
-                         void* workspace, size_t workspace_bytes, void* stream);
+                         const float* qp, int B, int H, int H_kv, int N, int D, int k_eff,
+                         float eps, void* O, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Decode prologue of one step, in one launch: RoPE of the step's projected q [B, H, D] and
+ * k [B, H_kv, D] rows with the model's position embeddings cos, sin [B, D] (HF
+ * apply_rotary_pos_emb, dcr_attention/models/llama/compat.py:63, evaluated op by op in
+ * the dtype like torch), the rotated query into q_out [B, H, D], the rotated key and v
+ * [B, H_kv, D] into K_cache / V_cache at position pos (replacing cache_update's torch.cat,
+ * compat.py:208); optionally (P given) the key's projection into KP_cache at pos and the
+ * projected unit queries into qp_out [B*H][R] fp32 for dcr_decode_projected. q, k, v are
+ * contiguous. */
+int dcr_decode_prologue(const void* q, const void* k, const void* v, const void* cos,
+                        const void* sin, int dtype, int B, int H, int H_kv, int D, void* q_out,
+                        void* K_cache, void* V_cache, int64_t c_stride_b, int64_t c_stride_h,
+                        int pos, int N_max, const float* P, int R, void* KP_cache,
+                        int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
+                        void* stream);
 
 /* ---------------------------------------------------------------------------------
  * Sequence-sharded decode over several GPUs (exact global top-K).

@@ -70,8 +70,8 @@ def test_projected_select_and_decode_vs_oracle(oracle_mod, cuda_lib, dt, B, H, H
     scores = torch.empty(B * H, N, dtype=torch.int16, device=DEV)
     psb, psh = KP.stride(0), KP.stride(1)
     st = cuda_lib.dcr_score_projected(KP.data_ptr(), _lib.DTYPE_CODES[dt], psb, psh,
-                                      Qd.data_ptr(), 1e-12, Pd.data_ptr(), 16, B, H, H_kv, N,
-                                      64, scores.data_ptr(), N, None)
+                                      Qd.data_ptr(), 1e-12, Pd.data_ptr(), 16, None, B, H, H_kv,
+                                      N, 64, scores.data_ptr(), N, None)
     assert st == 0
     assert np.array_equal(scores.cpu().numpy().view(np.uint16), s)
     sel = topk_qaxis_select_projected(Qd, KP, Pd, k)
