@@ -211,7 +211,6 @@ int dcr_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k
   if (w.splits > 1) {
     if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
     if (!aligned16(workspace)) return DCR_ERR_ALIGN;
-  if (!aligned16(workspace)) return DCR_ERR_ALIGN;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     partials = reinterpret_cast<float*>(ws + w.partials);
     counters = reinterpret_cast<int*>(ws + w.counters);
@@ -294,8 +293,7 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto mark = [&](int i) -> int {
     if (events == nullptr) return DCR_OK;
-    return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess ? DCR_OK
-                                                                                 : DCR_ERR_CUDA;
+    return record_mark(events[i], s);
   };
   if ((st = mark(0))) return st;
   // Pass 1 stores order keys, which Pass 2 reads directly.

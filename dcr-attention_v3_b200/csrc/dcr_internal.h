@@ -16,6 +16,19 @@ struct PeerView;  // dcr_peer.cuh
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 
+// Records a timing event on stream s. Inside a stream capture the record becomes an
+// external event-record node of the graph, so every replay of the graph stamps the event
+// (a plain record there only orders the capture and is never timed).
+inline int record_mark(void* event, cudaStream_t s) {
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess) return DCR_ERR_CUDA;
+  const cudaError_t e =
+      cap == cudaStreamCaptureStatusActive
+          ? cudaEventRecordWithFlags(static_cast<cudaEvent_t>(event), s, cudaEventRecordExternal)
+          : cudaEventRecord(static_cast<cudaEvent_t>(event), s);
+  return e == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+}
+
 // Sets the dynamic shared-memory limit of a kernel once per (kernel, device).
 cudaError_t ensure_smem_attr(const void* func, int bytes);
 

@@ -119,8 +119,7 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   auto mark = [&](int i) -> int {
     if (events == nullptr) return DCR_OK;
-    return cudaEventRecord(static_cast<cudaEvent_t>(events[i]), s) == cudaSuccess ? DCR_OK
-                                                                                 : DCR_ERR_CUDA;
+    return record_mark(events[i], s);
   };
   if ((st = mark(0))) return st;
   if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N_local,
