@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  __shared__ float P_s[kP3Tile];
+  __shared__ float2 P_s[kP3Tile];  // {p, p}: one packed operand of the P.V FMA
   __shared__ float o_red[kWarps][kD];
   __shared__ float m_red[kWarps];
   __shared__ float l_red[kWarps];
@@ -251,8 +251,8 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
   // Per-warp online-softmax state: warp w owns rows 16w .. 16w+15 of every tile.
   float m_w = -INFINITY;
   float l_part = 0.0f;       // lanes with half == 0 accumulate their row's weights
-  float o0 = 0.0f, o1 = 0.0f;    // dims 2*lane, 2*lane+1 (even rows)
-  float o0b = 0.0f, o1b = 0.0f;  // (odd rows)
+  float2 oe = make_float2(0.0f, 0.0f);  // dims 2*lane, 2*lane+1 (even rows)
+  float2 oo = make_float2(0.0f, 0.0f);  // (odd rows)
   const int r_own = warp * 16 + (lane >> 1);
 
   for (int tt = 0; tt < ntiles; ++tt) {
@@ -272,21 +272,21 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
     const uint32_t kt_addr = smem_u32(kt);
     const uint32_t vt_addr = smem_u32(vt);
 
-    // ---- scores of the warp's 16 rows: dims [32*half, 32*half + 32) per lane ----
-    float acc0 = 0.0f, acc1 = 0.0f;
+    // ---- scores of the warp's 16 rows: dims [32*half, 32*half + 32) per lane; two
+    // chains (even and odd dims) advanced by one packed FMA ----
+    float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int c = 0; c < kHalfChunks; ++c) {
       float f[kPer];
       ElemTraits<T>::widen(lds128(kt_addr + swz_offset(r_own, half * kHalfChunks + c, kP3Tile)), f);
 #pragma unroll
-      for (int e = 0; e < kPer; e += 2) {
-        acc0 = fmaf(f[e], qf[c * kPer + e], acc0);
-        acc1 = fmaf(f[e + 1], qf[c * kPer + e + 1], acc1);
-      }
+      for (int e = 0; e < kPer; e += 2)
+        acc = ffma2(make_float2(f[e], f[e + 1]),
+                    make_float2(qf[c * kPer + e], qf[c * kPer + e + 1]), acc);
     }
     // z in log2 units: dot * (1/sqrt(64)) * log2(e); p = 2^(z - m) with m the warp's
     // reference point (its running maximum, kept unless a score exceeds it by 2^8).
-    float z = acc0 + acc1;
+    float z = acc.x + acc.y;
     z += __shfl_xor_sync(0xffffffffu, z, 1);
     z *= 0.125f * 1.4426950408889634f;
     const bool valid = tt * kP3Tile + r_own < cnt;
@@ -300,20 +300,20 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
       m_w = m_new;
     }
     const float pr = valid ? exp2f(z - m_w) : 0.0f;
-    if (half == 0) P_s[r_own] = pr;
+    if (half == 0) P_s[r_own] = make_float2(pr, pr);
     l_part = l_part * alpha + (half == 0 ? pr : 0.0f);
     __syncwarp();
 
     // ---- P.V over the warp's rows: lane owns dims 2*lane, 2*lane+1; even and odd rows
     // accumulate separately (shorter dependent chains) and are added after the loop ----
-    o0 *= alpha;
-    o1 *= alpha;
-    o0b *= alpha;
-    o1b *= alpha;
+    oe.x *= alpha;
+    oe.y *= alpha;
+    oo.x *= alpha;
+    oo.y *= alpha;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int rr = warp * 16 + i;
-      const float pw = P_s[rr];
+      const float2 pw = P_s[rr];
       float2 v2;
       if constexpr (sizeof(T) == 4) {
         const uint32_t addr = vt_addr + swz_offset(rr, lane >> 1, kP3Tile) + (lane & 1) * 8;
@@ -324,17 +324,14 @@ __global__ void __launch_bounds__(kP3Threads, P3Cfg<T>::kMinBlocks)
         asm volatile("ld.shared.u32 %0, [%1];" : "=r"(w) : "r"(addr));
         v2 = ElemTraits<T>::widen2(w);
       }
-      if (i & 1) {
-        o0b = fmaf(pw, v2.x, o0b);
-        o1b = fmaf(pw, v2.y, o1b);
-      } else {
-        o0 = fmaf(pw, v2.x, o0);
-        o1 = fmaf(pw, v2.y, o1);
-      }
+      if (i & 1)
+        oo = ffma2(pw, v2, oo);
+      else
+        oe = ffma2(pw, v2, oe);
     }
   }
-  o0 += o0b;
-  o1 += o1b;
+  const float o0 = oe.x + oo.x;
+  const float o1 = oe.y + oo.y;
   if constexpr (!kTma) cp_async_wait<0>();
 
   // ---- merge the 4 warps' (m, l, o) ----

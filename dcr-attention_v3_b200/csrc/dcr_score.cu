@@ -140,20 +140,6 @@ __host__ __device__ constexpr int p1_ctas_per_sm() {
                     : (233472 / (p1_smem_bytes<T, G>() + 1024)));
 }
 
-// Two IEEE fused multiply-adds in one instruction: {a.x*b.x + c.x, a.y*b.y + c.y}.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  float2 d;
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
-      "mov.b64 ra, {%2, %3};\n\t"
-      "mov.b64 rb, {%4, %5};\n\t"
-      "mov.b64 rc, {%6, %7};\n\t"
-      "fma.rn.f32x2 rd, ra, rb, rc;\n\t"
-      "mov.b64 {%0, %1}, rd;\n\t}"
-      : "=f"(d.x), "=f"(d.y)
-      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-  return d;
-}
-
 struct P1Params {
   const float* u;  // [rows_q, 64] fp32 or nullptr (then computed from q)
   const void* q;   // [rows_q, 64] in the cache dtype
