@@ -32,6 +32,9 @@ namespace cg = cooperative_groups;
 
 namespace dcr {
 
+#ifndef DCR_P2_WIDE
+#define DCR_P2_WIDE 1
+#endif
 constexpr int kP2Threads = 512;
 constexpr int kP2Warps = kP2Threads / 32;
 constexpr int kP2MaxCluster = 8;
@@ -59,13 +62,14 @@ __device__ __forceinline__ uint32_t order_key_fast(uint32_t x) {
 }
 
 // VPT: vectors (8 positions each) per thread, 1..8.
-template <int VPT>
-__global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p) {
+template <int VPT, int TPB>
+__global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
+  constexpr int kWarpsB = TPB / 32;
   constexpr int kKeys = VPT * 8;
   constexpr int kWords = (kKeys + 31) / 32;
   __shared__ uint32_t hist_hi[256];
   __shared__ uint32_t hist_lo[256];
-  __shared__ uint32_t wsum[kP2Warps];
+  __shared__ uint32_t wsum[kWarpsB];
   __shared__ uint32_t scan_tot;
   __shared__ uint32_t cta_gt[kP2MaxCluster];
   __shared__ uint32_t cta_eq[kP2MaxCluster];
@@ -201,10 +205,10 @@ __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p)
   if (lane == 31) wsum[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t ws = lane < kP2Warps ? wsum[lane] : 0u;
+    const uint32_t ws = lane < kWarpsB ? wsum[lane] : 0u;
     const uint32_t wi = warp_incl_scan(ws);
-    if (lane < kP2Warps) wsum[lane] = wi - ws;
-    if (lane == kP2Warps - 1) scan_tot = wi;
+    if (lane < kWarpsB) wsum[lane] = wi - ws;
+    if (lane == kWarpsB - 1) scan_tot = wi;
   }
   __syncthreads();
   const uint32_t ex = incl - packed + wsum[warp];
@@ -254,10 +258,10 @@ __global__ void __launch_bounds__(kP2Threads, 1) select_kernel(const P2Params p)
   if (C > 1) cluster.sync();  // CTA 0's shared memory stays alive until all reads are done
 }
 
-template <int VPT>
+template <int VPT, int TPB>
 static int launch_select_t(const P2Params& p, int rows, int C, cudaStream_t st) {
-  return launch_cluster(select_kernel<VPT>, dim3(static_cast<unsigned>(rows * C)),
-                        dim3(kP2Threads), 0, st, C, p) == cudaSuccess
+  return launch_cluster(select_kernel<VPT, TPB>, dim3(static_cast<unsigned>(rows * C)),
+                        dim3(TPB), 0, st, C, p) == cudaSuccess
              ? DCR_OK
              : DCR_ERR_CUDA;
 }
@@ -282,11 +286,17 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   while (C < kP2MaxCluster && nvec > C * kP2Threads * 8) C *= 2;
   if (nvec > C * kP2Threads * 8) return DCR_ERR_SHAPE;  // more than 262144 positions per row
   p.seg_vec = (nvec + C - 1) / C;
+#if DCR_P2_WIDE
+  // One CTA per row and every row on its own SM: 1024 threads with half the keys each
+  // (up to 32 per thread, which fit the 64 registers a 1024-thread CTA allows).
+  if (C == 1 && rows <= sms && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4)
+    return launch_select_t<4, 1024>(p, rows, C, st);
+#endif
   const int vpt = (p.seg_vec + kP2Threads - 1) / kP2Threads;
-  if (vpt <= 1) return launch_select_t<1>(p, rows, C, st);
-  if (vpt <= 2) return launch_select_t<2>(p, rows, C, st);
-  if (vpt <= 4) return launch_select_t<4>(p, rows, C, st);
-  return launch_select_t<8>(p, rows, C, st);
+  if (vpt <= 1) return launch_select_t<1, kP2Threads>(p, rows, C, st);
+  if (vpt <= 2) return launch_select_t<2, kP2Threads>(p, rows, C, st);
+  if (vpt <= 4) return launch_select_t<4, kP2Threads>(p, rows, C, st);
+  return launch_select_t<8, kP2Threads>(p, rows, C, st);
 }
 
 }  // namespace dcr
