@@ -97,6 +97,14 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   int* bh0 = clustered ? cluster.map_shared_rank(&s_bh, 0) : &s_bh;
   uint32_t* above0 = clustered ? cluster.map_shared_rank(&s_above, 0) : &s_above;
 
+  // A one-CTA row needs only a block barrier between the phases.
+  auto row_sync = [&]() {
+    if (clustered)
+      cluster.sync();
+    else
+      __syncthreads();
+  };
+
   if (crank == 0 && tid == 0 && p.row_counters != nullptr) p.row_counters[row] = 0;
   if (tid < 256) {
     hist_lo[tid] = 0;
@@ -134,7 +142,7 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
       }
     }
   }
-  cluster.sync();  // histograms initialised everywhere before anyone adds into CTA 0's
+  row_sync();  // histograms initialised everywhere before anyone adds into CTA 0's
 
   // ---- level 1: histogram of the high byte, added into CTA 0 -------------------------
 #pragma unroll
@@ -144,7 +152,7 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
     __syncthreads();
     if (crank != 0 && tid < 256 && hist_hi[tid]) atomicAdd(hist_hi0 + tid, hist_hi[tid]);
   }
-  cluster.sync();
+  row_sync();
   if (crank == 0 && warp == 0) {
     int bin;
     uint32_t above;
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
       s_above = above;
     }
   }
-  cluster.sync();
+  row_sync();
   const uint32_t bh = static_cast<uint32_t>(*bh0);
 
   // ---- level 2: low byte of the keys in BH --------------------------------------------
@@ -165,7 +173,7 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
     __syncthreads();
     if (crank != 0 && tid < 256 && hist_lo[tid]) atomicAdd(hist_lo0 + tid, hist_lo[tid]);
   }
-  cluster.sync();
+  row_sync();
 
   // T and need: every CTA's warp 0 scans CTA 0's low-byte histogram
   __shared__ uint32_t s_T;
@@ -220,7 +228,7 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
       gt0[crank] = scan_tot & 0xffffu;
       eq0[crank] = scan_tot >> 16;
     }
-    cluster.sync();
+    row_sync();
     for (int c = 0; c < crank; ++c) {
       gt_before += gt0[c];
       eq_before_cta += eq0[c];
