@@ -359,13 +359,15 @@ def run_gpu_arm(args):
         del g2
         return a.elapsed_time(z)
 
-    # Each pass alone through its C-ABI entry (dcr_score, dcr_select, dcr_attend) over the
-    # same rotating layers: `steps` launches replayed as one CUDA graph with CUDA events only
-    # around the replay, i.e. the average launch duration back to back. (dcr_attend adds a
-    # 512-byte memset node per call for its split-K tickets, which the fused step does in
-    # Pass 2.) Events recorded between the passes inside the step graph are not used for
-    # this: each event-record node costs a few microseconds that land in the passes'
-    # intervals; that split is reported beside the standalone times.
+    # Per-pass time inside the step, from prefixes of the step replayed as CUDA graphs over
+    # the same rotating layers (`steps` calls per graph, CUDA events only around the
+    # replay): Pass 1 = dcr_score alone; Pass 2 = dcr_select_indices (Passes 1 and 2, the
+    # step's first two kernels) minus Pass 1; Pass 3 = the step (dcr_decode) minus Passes
+    # 1-2. Each pass's figure is its marginal device time in the back-to-back step, launch
+    # gap included. Also reported: Passes 2 and 3 alone through dcr_select and dcr_attend
+    # (the latter adds a memset node per call for its split-K tickets). Events recorded
+    # between the passes inside the step graph are not used: each event-record node costs
+    # a few microseconds that land in the passes' intervals; that split is reported too.
     sc_layers = [torch.empty(B * H, N, dtype=torch.int16, device=dev) for _ in range(LAYERS)]
     idx_layers = [torch.empty(B * H, k, dtype=torch.int32, device=dev) for _ in range(LAYERS)]
 
@@ -390,12 +392,23 @@ def run_gpu_arm(args):
         if st:
             raise _lib.DCRError(st, "dcr_attend")
 
+    def passes12(i, sptr):
+        K, _ = caches[i % LAYERS]
+        st = lib.dcr_select_indices(Qs[i % Qs.shape[0]].data_ptr(), K.data_ptr(), dcode, ksb,
+                                    ksh, B, H, H_kv, N, D, k, 1e-12, idx.data_ptr(),
+                                    ws.data_ptr(), ws_n, sptr)
+        if st:
+            raise _lib.DCRError(st, "dcr_select_indices")
+
     for i in range(LAYERS):  # selections of the layers' own queries for pass3_alone
         pass1_alone(i, sp)
         pass2_alone(i, sp)
-    p1 = graph_ms(pass1_alone) * 1e3 / steps
-    p2 = graph_ms(pass2_alone) * 1e3 / steps
-    p3 = graph_ms(pass3_alone) * 1e3 / steps
+    t1 = graph_ms(pass1_alone) * 1e3 / steps
+    t12 = graph_ms(passes12) * 1e3 / steps
+    t123 = graph_ms(step) * 1e3 / steps
+    p1, p2, p3 = t1, t12 - t1, t123 - t12
+    p2_alone = graph_ms(pass2_alone) * 1e3 / steps
+    p3_alone = graph_ms(pass3_alone) * 1e3 / steps
 
     # the step graph with CUDA events between its passes (external event-record nodes)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
@@ -409,18 +422,18 @@ def run_gpu_arm(args):
     with torch.cuda.graph(g3, stream=cap3):
         for i in range(steps):
             step_instrumented(i, evs[i], cap3.cuda_stream)
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
+    ev_a = torch.cuda.Event(enable_timing=True)
+    ev_b = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(cap3):
         g3.replay()  # warm replay
         barrier()
-        t0.record(cap3)
+        ev_a.record(cap3)
         g3.replay()
-        t1.record(cap3)
+        ev_b.record(cap3)
     barrier()
     del g3
     split = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) * 1e3 for j in range(3)]
-    evented_step = t0.elapsed_time(t1) * 1e3 / steps
+    evented_step = ev_a.elapsed_time(ev_b) * 1e3 / steps
     status = _lib.read_device_status(clear=True)
 
     # union of the selected rows per (b, h_kv): Pass 3's algorithmic K/V bytes
@@ -450,8 +463,13 @@ def run_gpu_arm(args):
     }
     for v in kern.values():
         v["frac_of_hbm"] = round(v["gbs"] / peak, 3)
-    kern["method"] = ("each pass alone through its C-ABI entry, steps launches replayed as one "
-                      "CUDA graph, events around the replay")
+    kern["method"] = ("marginal time in the step: graphs of dcr_score, dcr_select_indices "
+                      "(passes 1-2) and dcr_decode (passes 1-3), steps calls each, events "
+                      "around the replay; pass 2 = t12 - t1, pass 3 = t123 - t12")
+    kern["prefix_graphs_us"] = {"pass1": round(t1, 2), "passes12": round(t12, 2),
+                                "step": round(t123, 2)}
+    kern["alone_us"] = {"pass2_dcr_select": round(p2_alone, 2),
+                        "pass3_dcr_attend": round(p3_alone, 2)}
     kern["step_event_split_us"] = {
         "pass1": round(split[0], 2), "pass2": round(split[1], 2), "pass3": round(split[2], 2),
         "step_with_events_us": round(evented_step, 2),
