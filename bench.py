@@ -555,6 +555,10 @@ def run_gpu_arm(args):
     barrier()
     e2e_eager_ms = f0.elapsed_time(f1)
 
+    model_e2e = None
+    if world == 1 and not args.no_model:
+        model_e2e = model_decode_bench(dev, args.model_steps, stream)
+
     # max over ranks
     t = torch.tensor([ms, e2e_ms, ms_eager, e2e_eager_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -602,6 +606,7 @@ def run_gpu_arm(args):
                 "eager_api_value": round(e2e_eager_ms * 1e3 / (steps * world), 3),
                 "eager_api": "dcr_b200.kernel.cuda.topk_qaxis_attention called per step, "
                              "pinned host Q in / O out, host sync per step"},
+        "model_e2e": model_e2e,
         "gpu_launches": 3 * steps,
         "device_status": status,
         "clocks": clocks,
@@ -612,6 +617,64 @@ def run_gpu_arm(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def model_decode_bench(dev, n_steps, stream):
+    """Config 2: greedy decode of the 16-layer Llama-3.2-1B-architecture model (random-init
+    bf16 weights) from caches prefilled with N=32768 synthetic positions, B=4, c=0.15.
+
+    Each step is one CUDA graph (the H2D copy of the step's tokens from a pinned buffer, 16
+    layers, the tied LM head and argmax, the D2H copy of the next tokens) replayed with a
+    host sync, as a serving loop would; `n_steps` steps are timed with CUDA events on the
+    replay stream after one untimed run of the same steps. Reported for the exact and the
+    projected sparse modes and for dense SDPA in every layer (the reference's SDPA
+    baseline), on the same caches and weights."""
+    import torch
+
+    from dcr_b200.models.llama.model import DCRLlamaDecoder, GreedyDecodeGraphs
+    from dcr_b200.synthetic import projection_matrix
+    B, N0 = 4, 32768
+    model = DCRLlamaDecoder(attention="dcr", dtype=torch.bfloat16, device=dev, seed=0)
+    caches = model.new_caches(B, N0 + n_steps + 1, P=projection_matrix(seed=0, device=dev))
+    model.prefill_synthetic(caches, N0, seed=100)
+    first = torch.randint(0, model.cfg.vocab, (B,), generator=torch.Generator().manual_seed(0))
+    out = {}
+    tokens = {}
+    for name, attention, mode in [("dcr_exact", "dcr", "exact"),
+                                  ("dcr_projected", "dcr", "projected"),
+                                  ("dense_sdpa", "dense", "exact")]:
+        model.set_attention(attention)
+        for layer in model.layers:
+            layer.self_attn.mode = mode
+        for c in caches:  # every mode decodes the same positions of the same prefill
+            c.length = N0
+        runner = GreedyDecodeGraphs(model, caches, n_steps)
+        runner.run(first)  # untimed pass over the same steps
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        a.record(runner.stream)
+        toks = runner.run(first)
+        z.record(runner.stream)
+        torch.cuda.synchronize(dev)
+        out[name] = round(a.elapsed_time(z) / n_steps, 4)
+        tokens[name] = toks
+        runner.close()
+        del runner
+    del caches, model
+    torch.cuda.empty_cache()
+    return {
+        "ms_per_step": out, "unit": "ms/step",
+        "workload": "config2: Llama-3.2-1B architecture (16 layers, hidden 2048, FFN 8192 "
+                    "SwiGLU, 32 q / 8 KV heads of 64, vocab 128256, tied head), random-init "
+                    "bf16, B=4, caches prefilled with N=32768 synthetic positions, "
+                    f"{n_steps} greedy steps, c=0.15 (k_eff = adaptive_k_window(64, N, 0.15))",
+        "api": "dcr_b200.models.llama.model.GreedyDecodeGraphs: one CUDA graph per step "
+               "(H2D tokens, 16 layers, LM head, argmax, D2H tokens), host sync per step",
+        "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+        "greedy_tokens_agree_exact_vs_dense": float(
+            (tokens["dcr_exact"] == tokens["dense_sdpa"]).float().mean()),
+    }
 
 
 def run_sharded_arm(args):
@@ -889,6 +952,9 @@ def main():
     ap.add_argument("--soak", type=float, default=1.5, help="untimed seconds before timing")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the 16-layer model decode (config 2) measurement")
+    ap.add_argument("--model-steps", type=int, default=64)
     ap.add_argument("--split", choices=["seq", "heads"], default="seq",
                     help="multi-GPU layout: context split by sequence (weak scaling, exact "
                          "global top-K) or KV heads split (strong scaling)")

@@ -7,6 +7,7 @@
 #include "dcr_shard.cu"
 #include "dcr_project.cu"
 #include "dcr_rope.cu"
+#include "dcr_decode_ops.cu"
 #include "dcr_capi.cu"
 #include "dcr_peer_capi.cu"
 #include "dcr_noalloc.cu"

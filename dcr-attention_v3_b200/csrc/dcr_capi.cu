@@ -9,6 +9,7 @@
 
 #include <math.h>
 #include <mutex>
+#include <map>
 #include <set>
 #include <utility>
 
@@ -33,14 +34,15 @@ int device_sm_count() {
 
 cudaError_t ensure_smem_attr(const void* func, int bytes) {
   static std::mutex mu;
-  static std::set<std::pair<const void*, int>> done;
+  static std::map<std::pair<const void*, int>, int> limit;  // the largest size set so far
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(mu);
-  if (done.count({func, dev})) return cudaSuccess;
+  auto it = limit.find({func, dev});
+  if (it != limit.end() && it->second >= bytes) return cudaSuccess;
   e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) done.insert({func, dev});
+  if (e == cudaSuccess) limit[{func, dev}] = bytes;
   return e;
 }
 

@@ -299,6 +299,12 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   // (up to 32 per thread, which fit the 64 registers a 1024-thread CTA allows).
   if (C == 1 && rows <= sms && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4)
     return launch_select_t<4, 1024>(p, rows, C, st);
+  // Just past 32768 positions a two-CTA cluster per row would need two waves for 128
+  // rows: one 1024-thread CTA with 40 keys per thread covers up to 40960 positions.
+  if (rows <= sms && nvec > 1024 * 4 && nvec <= 1024 * 5) {
+    p.seg_vec = nvec;
+    return launch_select_t<5, 1024>(p, rows, 1, st);
+  }
 #endif
   const int vpt = (p.seg_vec + kP2Threads - 1) / kP2Threads;
   if (vpt <= 1) return launch_select_t<1, kP2Threads>(p, rows, C, st);

@@ -68,8 +68,10 @@ class DCRDecodeAttention(torch.nn.Module):
 
     def __init__(self, hidden: int, H: int, H_kv: int, *, k_window: int = 64,
                  coverage_floor: float = 0.15, T_dispatch: int = 4096, mode: str = "exact",
-                 dtype: torch.dtype = torch.bfloat16, device="cuda", eps: float = 1e-12):
+                 dtype: torch.dtype = torch.bfloat16, device="cuda", eps: float = 1e-12,
+                 fast_linear: bool = False):
         super().__init__()
+        self.fast_linear = fast_linear
         require(mode in ("exact", "projected"), f"mode must be 'exact' or 'projected', got {mode}")
         require(H % H_kv == 0, "H must be a multiple of H_kv")
         self.hidden, self.H, self.H_kv = hidden, H, H_kv
@@ -89,10 +91,9 @@ class DCRDecodeAttention(torch.nn.Module):
         k_eff = adaptive_k_window(self.k_window, N_kv, self.coverage_floor)
         if N_kv < self.T_dispatch or k_eff >= N_kv:
             self.last_branch = "sdpa"
-            G = self.H // self.H_kv
-            K = cache.K.repeat_interleave(G, dim=1)
-            V = cache.V.repeat_interleave(G, dim=1)
-            return F.scaled_dot_product_attention(q_rot[:, :, None], K, V).squeeze(2)
+            # query head h reads KV head h // G, as the reference's repeat_kv (no copy)
+            return F.scaled_dot_product_attention(q_rot[:, :, None], cache.K, cache.V,
+                                                  enable_gqa=True).squeeze(2)
         self.last_branch = "dcr"
         if self.mode == "projected":
             from dcr_b200.kernel.cuda.projected import topk_qaxis_attention_projected
@@ -101,6 +102,14 @@ class DCRDecodeAttention(torch.nn.Module):
         from dcr_b200.kernel.cuda.topk_axis import topk_qaxis_attention
         return topk_qaxis_attention(q_rot, cache.K, cache.V, k_eff, eps=self.eps)
 
+    def proj(self, x: torch.Tensor, lin: torch.nn.Linear) -> torch.Tensor:
+        """``lin(x)``; with ``fast_linear`` through the skinny decode GEMM when it applies."""
+        if self.fast_linear:
+            from dcr_b200.kernel.cuda.decode_ops import linear_skinny, skinny_ok
+            if skinny_ok(x, lin.weight):
+                return linear_skinny(x, lin.weight)
+        return lin(x)
+
     def forward(self, hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                 cache: StaticKVCache) -> torch.Tensor:
         """hidden_states [B, 1, hidden], cos/sin [B, 1, D] (the model's position embeddings
@@ -108,14 +117,14 @@ class DCRDecodeAttention(torch.nn.Module):
         B, n_q, _ = hidden_states.shape
         require(n_q == 1, "decode step: one new token per sequence")
         x = hidden_states[:, 0]
-        q = self.q_proj(x).view(B, self.H, HEAD_DIM)
-        k = self.k_proj(x).view(B, self.H_kv, HEAD_DIM)
-        v = self.v_proj(x).view(B, self.H_kv, HEAD_DIM)
+        q = self.proj(x, self.q_proj).view(B, self.H, HEAD_DIM)
+        k = self.proj(x, self.k_proj).view(B, self.H_kv, HEAD_DIM)
+        v = self.proj(x, self.v_proj).view(B, self.H_kv, HEAD_DIM)
         q_rot, qp = cache.append_rotated(q, k, v, cos.reshape(B, HEAD_DIM),
                                          sin.reshape(B, HEAD_DIM),
                                          want_qp=self.mode == "projected", eps=self.eps)
         O = self.attend(q_rot, qp, cache)
-        return self.o_proj(O.reshape(B, 1, self.H * HEAD_DIM))
+        return self.proj(O.reshape(B, 1, self.H * HEAD_DIM), self.o_proj)
 
 
 class KVHeadParallelDecodeAttention(DCRDecodeAttention):

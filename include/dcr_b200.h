@@ -337,6 +337,29 @@ int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int
  * Diagnostic: the reference has no counterpart (its kernels have no device status). */
 int dcr_read_device_status(int* status_out, int clear);
 
+/* ---- the rest of a decode step (dcr_decode_ops.cu) -----------------------------------
+ * Kernels for the layers around the attention in a decode model (HF LlamaRMSNorm, the
+ * residual adds, LlamaMLP's SiLU-gated product, nn.Linear for a few tokens), with torch's
+ * rounding of the same op sequence. All pointers are device pointers, row-major and
+ * contiguous; dtype is a dcr_dtype. */
+
+/* h_out = h + delta (rounded to dtype; delta may be NULL: no add, h_out unused; h_out may
+ * equal h), then y = weight * dtype(h_out * rsqrt(mean(h_out^2) + eps)) per row of `dim`.
+ * Replaces the residual add and LlamaRMSNorm.forward (transformers modeling_llama). */
+int dcr_add_rmsnorm(const void* h, const void* delta, const void* weight, int dtype, int rows,
+                    int dim, float eps, void* h_out, void* y, void* stream);
+
+/* out = dtype(dtype(silu(gate)) * up) elementwise over n values (LlamaMLP's act_fn(gate) * up). */
+int dcr_silu_mul(const void* gate, const void* up, int dtype, int64_t n, void* out,
+                 void* stream);
+
+#define DCR_SKINNY_MAX_M 8
+/* y[M][N] = x[M][K] . weight[N][K]^T for 1 <= M <= DCR_SKINNY_MAX_M tokens (nn.Linear
+ * without bias, weight in nn.Linear's layout), fp32 accumulation, 16-bit dtype only;
+ * K a multiple of 256, x and weight 16-byte aligned. */
+int dcr_linear_skinny(const void* x, const void* weight, int dtype, int M, int N, int K,
+                      void* y, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

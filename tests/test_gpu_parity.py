@@ -128,6 +128,9 @@ SWEEP = [
     (1, 32, 8, 20000, 1, "f16"),
     (2, 64, 8, 3000, 450, "bf16"),       # G = 8
     (1, 32, 8, 4096, 614, "f32"),        # config 0
+    (4, 32, 8, 32771, 4916, "bf16"),     # just past 32768: one 1024-thread CTA per row
+    (4, 32, 8, 40960, 6144, "f16"),      # the longest row that shape covers
+    (4, 32, 8, 40961, 6144, "bf16"),     # two-CTA clusters
 ]
 
 
