@@ -421,13 +421,17 @@ int dcr_decode_projected(const void* Q, const void* K, const void* V, const void
                      N, D, k_eff, eps, O, workspace, workspace_bytes, stream, nullptr, &proj);
 }
 
-int dcr_decode_prologue(const void* q, const void* k, const void* v, const void* cos,
-                        const void* sin, int dtype, int B, int H, int H_kv, int D, void* q_out,
-                        void* K_cache, void* V_cache, int64_t c_stride_b, int64_t c_stride_h,
-                        int pos, int N_max, const float* P, int R, void* KP_cache,
-                        int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
-                        void* stream) {
+int dcr_decode_prologue_strided(const void* q, const void* k, const void* v, int64_t in_sb_q,
+                                int64_t in_sb_kv, const void* cos, const void* sin, int dtype,
+                                int B, int H, int H_kv, int D, void* q_out, void* K_cache,
+                                void* V_cache, int64_t c_stride_b, int64_t c_stride_h, int pos,
+                                int N_max, const float* P, int R, void* KP_cache,
+                                int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
+                                void* stream) {
   if (B <= 0 || H <= 0 || H_kv <= 0 || N_max <= 0 || D != kD || H % H_kv != 0)
+    return DCR_ERR_SHAPE;
+  if (in_sb_q < 0 || in_sb_kv < 0 || (in_sb_q > 0 && in_sb_q < static_cast<int64_t>(H) * kD) ||
+      (in_sb_kv > 0 && in_sb_kv < static_cast<int64_t>(H_kv) * kD))
     return DCR_ERR_SHAPE;
   if (pos < 0 || pos >= N_max) return DCR_ERR_SHAPE;
   if (q == nullptr || k == nullptr || v == nullptr || cos == nullptr || sin == nullptr ||
@@ -445,7 +449,18 @@ int dcr_decode_prologue(const void* q, const void* k, const void* v, const void*
     return st;
   return launch_rope_append(q, k, v, cos, sin, dtype, B, H, H_kv, q_out, K_cache, V_cache,
                             c_stride_b, c_stride_h, pos, KP_cache, p_stride_b, p_stride_h, P,
-                            qp_out, eps, static_cast<cudaStream_t>(stream));
+                            qp_out, eps, static_cast<cudaStream_t>(stream), in_sb_q, in_sb_kv);
+}
+
+int dcr_decode_prologue(const void* q, const void* k, const void* v, const void* cos,
+                        const void* sin, int dtype, int B, int H, int H_kv, int D, void* q_out,
+                        void* K_cache, void* V_cache, int64_t c_stride_b, int64_t c_stride_h,
+                        int pos, int N_max, const float* P, int R, void* KP_cache,
+                        int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
+                        void* stream) {
+  return dcr_decode_prologue_strided(q, k, v, 0, 0, cos, sin, dtype, B, H, H_kv, D, q_out,
+                                     K_cache, V_cache, c_stride_b, c_stride_h, pos, N_max, P, R,
+                                     KP_cache, p_stride_b, p_stride_h, qp_out, eps, stream);
 }
 
 // ---- sequence-sharded decode ----------------------------------------------------------

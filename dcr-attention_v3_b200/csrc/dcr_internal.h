@@ -136,11 +136,13 @@ int launch_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_
                            int H, int H_kv, int N, uint16_t* scores, int64_t s_stride,
                            int keys_out, cudaStream_t st);
 // Decode prologue (dcr_rope.cu): RoPE of the step's q and k rows, cache append at pos,
-// and (optional) KP of the new key row and the projected unit queries qp.
+// and (optional) KP of the new key row and the projected unit queries qp. q_sb / kv_sb:
+// elements between the batch rows of q and of k, v (0: contiguous [B, H or H_kv, D]).
 int launch_rope_append(const void* q, const void* k, const void* v, const void* cos,
                        const void* sin, int dtype, int B, int H, int H_kv, void* q_out,
                        void* k_cache, void* v_cache, int64_t csb, int64_t csh, int pos,
                        void* kp, int64_t psb, int64_t psh, const float* P, float* qp,
-                       float eps, cudaStream_t st);
+                       float eps, cudaStream_t st,
+                       int64_t q_sb = 0, int64_t kv_sb = 0);
 
 }  // namespace dcr

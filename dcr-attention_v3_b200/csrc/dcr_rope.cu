@@ -41,6 +41,7 @@ struct RopeParams {
   float* qp;           // optional [B, H, R] projected unit queries
   float eps;
   int H, H_kv;
+  int64_t q_sb, kv_sb;  // elements between the batch rows of q and of k/v
 };
 
 template <typename T>
@@ -82,9 +83,11 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_append_kernel(const Rope
     const bool is_q = head < p.H;
     const int h = is_q ? head : head - p.H;
     const void* src = is_q ? p.q : p.k;
+    const int64_t in_row = static_cast<int64_t>(b) * (is_q ? p.q_sb : p.kv_sb) +
+                           static_cast<int64_t>(h) * kD;
     const int64_t row = (static_cast<int64_t>(b) * (is_q ? p.H : p.H_kv) + h) * kD;
-    const float x0 = elem<T>(src, row + lane);
-    const float x1 = elem<T>(src, row + lane + 32);
+    const float x0 = elem<T>(src, in_row + lane);
+    const float x1 = elem<T>(src, in_row + lane + 32);
     // q*cos + rotate_half(q)*sin, each op rounded to T as torch evaluates it (the _rn
     // intrinsics keep fp32 from contracting the products into the sum)
     const float y0 = rope_round<T>(__fadd_rn(rope_round<T>(__fmul_rn(x0, c0)),
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(kRopeWarps * 32) rope_append_kernel(const Rope
       T* vc = static_cast<T*>(p.v_cache) + b * p.csb + h * p.csh + static_cast<int64_t>(p.pos) * kD;
       ElemTraits<T>::store(kc, lane, y0);
       ElemTraits<T>::store(kc, lane + 32, y1);
-      const int64_t vrow = (static_cast<int64_t>(b) * p.H_kv + h) * kD;
+      const int64_t vrow = static_cast<int64_t>(b) * p.kv_sb + static_cast<int64_t>(h) * kD;
       ElemTraits<T>::store(vc, lane, elem<T>(p.v, vrow + lane));
       ElemTraits<T>::store(vc, lane + 32, elem<T>(p.v, vrow + lane + 32));
       if (p.kp != nullptr && lane < kR) {
@@ -138,7 +141,7 @@ int launch_rope_append(const void* q, const void* k, const void* v, const void* 
                        const void* sin, int dtype, int B, int H, int H_kv, void* q_out,
                        void* k_cache, void* v_cache, int64_t csb, int64_t csh, int pos,
                        void* kp, int64_t psb, int64_t psh, const float* P, float* qp,
-                       float eps, cudaStream_t st) {
+                       float eps, cudaStream_t st, int64_t q_sb, int64_t kv_sb) {
   RopeParams p;
   p.q = q;
   p.k = k;
@@ -159,6 +162,8 @@ int launch_rope_append(const void* q, const void* k, const void* v, const void* 
   p.eps = eps;
   p.H = H;
   p.H_kv = H_kv;
+  p.q_sb = q_sb > 0 ? q_sb : static_cast<int64_t>(H) * kD;
+  p.kv_sb = kv_sb > 0 ? kv_sb : static_cast<int64_t>(H_kv) * kD;
   switch (dtype) {
     case DCR_DTYPE_BF16: rope_append_kernel<__nv_bfloat16><<<B, kRopeWarps * 32, 0, st>>>(p); break;
     case DCR_DTYPE_F16: rope_append_kernel<__half><<<B, kRopeWarps * 32, 0, st>>>(p); break;

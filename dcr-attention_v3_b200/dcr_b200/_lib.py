@@ -70,9 +70,12 @@ SIGNATURES = {
     "dcr_decode_prologue": (_i32, [_vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _vp,
                                    _vp, _vp, _i64, _i64, _i32, _i32, _vp, _i32, _vp, _i64, _i64,
                                    _vp, _f32, _vp]),
+    "dcr_decode_prologue_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32,
+                                           _i32, _i32, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
+                                           _vp, _i32, _vp, _i64, _i64, _vp, _f32, _vp]),
     "dcr_add_rmsnorm": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp]),
     "dcr_silu_mul": (_i32, [_vp, _vp, _i32, _i64, _vp, _vp]),
-    "dcr_linear_skinny": (_i32, [_vp, _vp, _i32, _i32, _i32, _i32, _vp, _vp]),
+    "dcr_silu_mul_packed": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp]),
     "dcr_shard_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32, _i32]),
     "dcr_shard_score": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32,
                                _f32, _vp, _vp, _sz, _vp]),

@@ -1,12 +1,12 @@
 """The layers around the attention in a decode step, on this package's kernels.
 
 A decode step of a Llama model runs, per layer, a residual add and HF ``LlamaRMSNorm``
-twice, four ``nn.Linear`` projections of the attention, the SwiGLU MLP and, at the end, a
-norm and the LM head (transformers' ``modeling_llama``; the reference keeps them in torch).
-With B = 1-8 tokens these are matrix-vector products and kilobyte-sized elementwise ops:
-:func:`linear_skinny` streams each weight once, :func:`add_rmsnorm` and :func:`silu_mul`
-replace the chains of small torch kernels with one launch each, with torch's rounding of the
-same op sequence (see ``csrc/dcr_decode_ops.cu``).
+twice, the attention's projections, the SwiGLU MLP and, at the end, a norm and the LM head
+(transformers' ``modeling_llama``; the reference keeps them in torch). With B = 1-8 tokens
+the norms and activations are kilobyte-sized: :func:`add_rmsnorm` and :func:`silu_mul`
+replace chains of small torch kernels with one launch each, with torch's rounding of the
+same op sequence (see ``csrc/dcr_decode_ops.cu``). :func:`pack_linears` lets one library
+GEMM compute several projections of the same input (q/k/v, gate/up).
 """
 from __future__ import annotations
 
@@ -16,9 +16,6 @@ import torch
 
 from dcr_b200 import _lib
 from dcr_b200.kernel.cuda._common import check_dtype, require
-
-SKINNY_MAX_M = 8
-
 
 def _dt(x: torch.Tensor) -> int:
     return check_dtype(x, "tensor")
@@ -65,31 +62,37 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def linear_skinny(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
-    """x [..., K] @ weight[N, K]^T for at most 8 rows of x (nn.Linear without bias),
-    16-bit dtypes, K a multiple of 256."""
-    _lib.require_cuda(x, weight)
-    K = x.shape[-1]
-    M = x.numel() // K
-    require(weight.dim() == 2 and weight.shape[1] == K, "weight must be [N, K]")
-    require(x.is_contiguous() and weight.is_contiguous(), "x and weight must be contiguous")
-    require(x.dtype == weight.dtype and x.dtype in (torch.bfloat16, torch.float16),
-            "x and weight must share a 16-bit dtype")
-    require(1 <= M <= SKINNY_MAX_M and K % 256 == 0,
-            f"need 1 <= rows <= {SKINNY_MAX_M} and K % 256 == 0, got rows={M}, K={K}")
-    N = weight.shape[0]
-    y = torch.empty(*x.shape[:-1], N, dtype=x.dtype, device=x.device)
-    with torch.cuda.device(x.device):
-        st = _lib.load().dcr_linear_skinny(x.data_ptr(), weight.data_ptr(), _dt(x), M, N, K,
-                                           y.data_ptr(), _lib.stream_ptr(x.device))
-    _lib.check(st, "dcr_linear_skinny")
-    return y
+def silu_mul_packed(gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up from one [..., 2 * inter] tensor holding gate then up (the output of
+    one GEMM over the concatenated gate and up weights) -> [..., inter]."""
+    _lib.require_cuda(gate_up)
+    require(gate_up.is_contiguous() and gate_up.shape[-1] % 2 == 0,
+            "gate_up must be contiguous with an even last dim")
+    inter = gate_up.shape[-1] // 2
+    rows = gate_up.numel() // gate_up.shape[-1]
+    out = torch.empty(*gate_up.shape[:-1], inter, dtype=gate_up.dtype, device=gate_up.device)
+    with torch.cuda.device(gate_up.device):
+        st = _lib.load().dcr_silu_mul_packed(gate_up.data_ptr(), _dt(gate_up), rows, inter,
+                                             out.data_ptr(), _lib.stream_ptr(gate_up.device))
+    _lib.check(st, "dcr_silu_mul_packed")
+    return out
 
 
-def skinny_ok(x: torch.Tensor, weight: torch.Tensor) -> bool:
-    """Whether :func:`linear_skinny` takes this product (else use a library GEMM)."""
-    K = x.shape[-1]
-    M = x.numel() // K
-    return (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and
-            weight.dtype == x.dtype and 1 <= M <= SKINNY_MAX_M and K % 256 == 0 and
-            x.is_contiguous() and weight.is_contiguous() and M * K * 2 <= 200 * 1024)
+def pack_linears(*layers: torch.nn.Linear) -> torch.Tensor:
+    """Puts the weights of bias-free linear layers over one input into one [sum N, K]
+    tensor and makes each layer's weight a view of its rows, so one GEMM computes all of
+    them (weights loaded later, e.g. by load_state_dict, land in the packed tensor)."""
+    K = layers[0].weight.shape[1]
+    require(all(l.weight.shape[1] == K and l.bias is None for l in layers),
+            "packed layers must share the input size and have no bias")
+    w0 = layers[0].weight
+    packed = torch.empty(sum(l.weight.shape[0] for l in layers), K, dtype=w0.dtype,
+                         device=w0.device)
+    r = 0
+    with torch.no_grad():
+        for l in layers:
+            n = l.weight.shape[0]
+            packed[r:r + n].copy_(l.weight)
+            l.weight = torch.nn.Parameter(packed[r:r + n], requires_grad=l.weight.requires_grad)
+            r += n
+    return packed

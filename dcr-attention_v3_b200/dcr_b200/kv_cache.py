@@ -84,7 +84,8 @@ class StaticKVCache:
     def append_rotated(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                        cos: torch.Tensor, sin: torch.Tensor, *, want_qp: bool = False,
                        eps: float = 1e-12) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
-        """The decode prologue of one step in one launch (dcr_decode_prologue): RoPE of the
+        """The decode prologue of one step in one launch (dcr_decode_prologue_strided; q, k, v
+        may be slices of one packed q/k/v row per batch entry): RoPE of the
         step's q [B, H, D] and k [B, H_kv, D] rows with the position embeddings cos, sin
         [B, D] (HF apply_rotary_pos_emb, dcr_attention/models/llama/compat.py:63), the
         rotated k and v appended at position ``length`` (with their projection when the
@@ -98,9 +99,15 @@ class StaticKVCache:
                 f"q, k, v, cos, sin must be {self.dtype}")
         require(tuple(cos.shape) == (B, D) and tuple(sin.shape) == (B, D), "cos, sin [B, D]")
         require(self.length < self.N_max, f"cache full: N_max={self.N_max}")
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+
+        def rows_ok(t):  # [B, h, D] with contiguous heads, any batch stride
+            return t.stride(-1) == 1 and (t.shape[1] == 1 or t.stride(1) == D)
+        if not rows_ok(q):
+            q = q.contiguous()
+        if not (rows_ok(k) and rows_ok(v) and k.stride(0) == v.stride(0)):
+            k, v = k.contiguous(), v.contiguous()
         cos, sin = cos.contiguous(), sin.contiguous()
-        q_out = torch.empty_like(q)
+        q_out = torch.empty(B, H, D, dtype=q.dtype, device=q.device)
         qp = None
         if want_qp:
             require(self.P is not None, "want_qp needs a cache with a projection P")
@@ -114,8 +121,9 @@ class StaticKVCache:
             kp_ptr = None
         P_ptr = self.P.data_ptr() if self.P is not None else None
         with torch.cuda.device(self.device):
-            st = _lib.load().dcr_decode_prologue(
-                q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+            st = _lib.load().dcr_decode_prologue_strided(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), q.stride(0) if B > 1 else 0,
+                k.stride(0) if B > 1 else 0, cos.data_ptr(), sin.data_ptr(),
                 _lib.DTYPE_CODES[self.dtype], B, H, self.H_kv, HEAD_DIM, q_out.data_ptr(),
                 self.k.data_ptr(), self.v.data_ptr(), csb, csh, self.length, self.N_max, P_ptr,
                 PROJ_RANK, kp_ptr, psb, psh, None if qp is None else qp.data_ptr(), float(eps),

@@ -69,9 +69,8 @@ class DCRDecodeAttention(torch.nn.Module):
     def __init__(self, hidden: int, H: int, H_kv: int, *, k_window: int = 64,
                  coverage_floor: float = 0.15, T_dispatch: int = 4096, mode: str = "exact",
                  dtype: torch.dtype = torch.bfloat16, device="cuda", eps: float = 1e-12,
-                 fast_linear: bool = False):
+                 pack_qkv: bool = False):
         super().__init__()
-        self.fast_linear = fast_linear
         require(mode in ("exact", "projected"), f"mode must be 'exact' or 'projected', got {mode}")
         require(H % H_kv == 0, "H must be a multiple of H_kv")
         self.hidden, self.H, self.H_kv = hidden, H, H_kv
@@ -83,6 +82,10 @@ class DCRDecodeAttention(torch.nn.Module):
         self.v_proj = torch.nn.Linear(hidden, H_kv * HEAD_DIM, **kw)
         self.o_proj = torch.nn.Linear(H * HEAD_DIM, hidden, **kw)
         self.last_branch = None
+        self._qkv = None
+        if pack_qkv:  # q/k/v weights as row views of one tensor: one GEMM for all three
+            from dcr_b200.kernel.cuda.decode_ops import pack_linears
+            self._qkv = pack_linears(self.q_proj, self.k_proj, self.v_proj)
 
     def attend(self, q_rot: torch.Tensor, qp: Optional[torch.Tensor],
                cache: StaticKVCache) -> torch.Tensor:
@@ -102,14 +105,6 @@ class DCRDecodeAttention(torch.nn.Module):
         from dcr_b200.kernel.cuda.topk_axis import topk_qaxis_attention
         return topk_qaxis_attention(q_rot, cache.K, cache.V, k_eff, eps=self.eps)
 
-    def proj(self, x: torch.Tensor, lin: torch.nn.Linear) -> torch.Tensor:
-        """``lin(x)``; with ``fast_linear`` through the skinny decode GEMM when it applies."""
-        if self.fast_linear:
-            from dcr_b200.kernel.cuda.decode_ops import linear_skinny, skinny_ok
-            if skinny_ok(x, lin.weight):
-                return linear_skinny(x, lin.weight)
-        return lin(x)
-
     def forward(self, hidden_states: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
                 cache: StaticKVCache) -> torch.Tensor:
         """hidden_states [B, 1, hidden], cos/sin [B, 1, D] (the model's position embeddings
@@ -117,14 +112,22 @@ class DCRDecodeAttention(torch.nn.Module):
         B, n_q, _ = hidden_states.shape
         require(n_q == 1, "decode step: one new token per sequence")
         x = hidden_states[:, 0]
-        q = self.proj(x, self.q_proj).view(B, self.H, HEAD_DIM)
-        k = self.proj(x, self.k_proj).view(B, self.H_kv, HEAD_DIM)
-        v = self.proj(x, self.v_proj).view(B, self.H_kv, HEAD_DIM)
+        nq, nk = self.H * HEAD_DIM, self.H_kv * HEAD_DIM
+        if self._qkv is not None:
+            # one GEMM; the prologue reads q, k, v as strided slices of its rows
+            qkv = F.linear(x, self._qkv)
+            q = qkv[:, :nq].view(B, self.H, HEAD_DIM)
+            k = qkv[:, nq:nq + nk].view(B, self.H_kv, HEAD_DIM)
+            v = qkv[:, nq + nk:].view(B, self.H_kv, HEAD_DIM)
+        else:
+            q = self.q_proj(x).view(B, self.H, HEAD_DIM)
+            k = self.k_proj(x).view(B, self.H_kv, HEAD_DIM)
+            v = self.v_proj(x).view(B, self.H_kv, HEAD_DIM)
         q_rot, qp = cache.append_rotated(q, k, v, cos.reshape(B, HEAD_DIM),
                                          sin.reshape(B, HEAD_DIM),
                                          want_qp=self.mode == "projected", eps=self.eps)
         O = self.attend(q_rot, qp, cache)
-        return self.proj(O.reshape(B, 1, self.H * HEAD_DIM), self.o_proj)
+        return self.o_proj(O.reshape(B, 1, self.H * HEAD_DIM))
 
 
 class KVHeadParallelDecodeAttention(DCRDecodeAttention):

@@ -72,11 +72,15 @@ class DecoderLayer(torch.nn.Module):
         self.self_attn = DCRDecodeAttention(
             cfg.hidden, cfg.heads, cfg.kv_heads, k_window=k_window, coverage_floor=coverage_floor,
             T_dispatch=(1 << 62) if attention == "dense" else T_dispatch, mode=mode, dtype=dtype,
-            device=device, fast_linear=fast)
+            device=device, pack_qkv=fast)
         self.post_attention_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps, dtype, device)
         self.gate_proj = torch.nn.Linear(cfg.hidden, cfg.intermediate, **kw)
         self.up_proj = torch.nn.Linear(cfg.hidden, cfg.intermediate, **kw)
         self.down_proj = torch.nn.Linear(cfg.intermediate, cfg.hidden, **kw)
+        self._gate_up = None
+        if fast:  # gate and up weights as row views of one tensor: one GEMM for both
+            from dcr_b200.kernel.cuda.decode_ops import pack_linears
+            self._gate_up = pack_linears(self.gate_proj, self.up_proj)
 
     def forward(self, h, delta, cos, sin, cache):
         """The layer on the residual stream h [B, 1, hidden] plus the previous layer's
@@ -89,13 +93,12 @@ class DecoderLayer(torch.nn.Module):
             h = h + self.self_attn(self.input_layernorm(h), cos, sin, cache)
             x = self.post_attention_layernorm(h)
             return h, self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
-        from dcr_b200.kernel.cuda.decode_ops import add_rmsnorm, silu_mul
+        from dcr_b200.kernel.cuda.decode_ops import add_rmsnorm, silu_mul_packed
         eps = self.input_layernorm.eps
         h, x = add_rmsnorm(h, delta, self.input_layernorm.weight, eps)
         a = self.self_attn(x, cos, sin, cache)
         h, x = add_rmsnorm(h, a, self.post_attention_layernorm.weight, eps)
-        p = self.self_attn.proj
-        return h, p(silu_mul(p(x, self.gate_proj), p(x, self.up_proj)), self.down_proj)
+        return h, self.down_proj(silu_mul_packed(F.linear(x, self._gate_up)))
 
 
 class DCRLlamaDecoder(torch.nn.Module):

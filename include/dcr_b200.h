@@ -229,6 +229,17 @@ int dcr_decode_prologue(const void* q, const void* k, const void* v, const void*
                         int64_t p_stride_b, int64_t p_stride_h, float* qp_out, float eps,
                         void* stream);
 
+/* The same with q, k and v rows read at in_stride_b_q / in_stride_b_kv elements between
+ * batch rows (0: contiguous), e.g. slices of one [B][(H + 2 H_kv) D] output of a GEMM over
+ * the concatenated q/k/v weights. q_out stays contiguous [B, H, D]. */
+int dcr_decode_prologue_strided(const void* q, const void* k, const void* v,
+                                int64_t in_stride_b_q, int64_t in_stride_b_kv, const void* cos,
+                                const void* sin, int dtype, int B, int H, int H_kv, int D,
+                                void* q_out, void* K_cache, void* V_cache, int64_t c_stride_b,
+                                int64_t c_stride_h, int pos, int N_max, const float* P, int R,
+                                void* KP_cache, int64_t p_stride_b, int64_t p_stride_h,
+                                float* qp_out, float eps, void* stream);
+
 /* ---------------------------------------------------------------------------------
  * Sequence-sharded decode over several GPUs (exact global top-K).
  *
@@ -339,8 +350,8 @@ int dcr_read_device_status(int* status_out, int clear);
 
 /* ---- the rest of a decode step (dcr_decode_ops.cu) -----------------------------------
  * Kernels for the layers around the attention in a decode model (HF LlamaRMSNorm, the
- * residual adds, LlamaMLP's SiLU-gated product, nn.Linear for a few tokens), with torch's
- * rounding of the same op sequence. All pointers are device pointers, row-major and
+ * residual adds, LlamaMLP's SiLU-gated product), with torch's rounding of the same op
+ * sequence. All pointers are device pointers, row-major and
  * contiguous; dtype is a dcr_dtype. */
 
 /* h_out = h + delta (rounded to dtype; delta may be NULL: no add, h_out unused; h_out may
@@ -353,12 +364,10 @@ int dcr_add_rmsnorm(const void* h, const void* delta, const void* weight, int dt
 int dcr_silu_mul(const void* gate, const void* up, int dtype, int64_t n, void* out,
                  void* stream);
 
-#define DCR_SKINNY_MAX_M 8
-/* y[M][N] = x[M][K] . weight[N][K]^T for 1 <= M <= DCR_SKINNY_MAX_M tokens (nn.Linear
- * without bias, weight in nn.Linear's layout), fp32 accumulation, 16-bit dtype only;
- * K a multiple of 256, x and weight 16-byte aligned. */
-int dcr_linear_skinny(const void* x, const void* weight, int dtype, int M, int N, int K,
-                      void* y, void* stream);
+/* The same from one [rows][2 * inter] tensor holding gate then up in each row (the output
+ * of one GEMM over the concatenated gate and up weights): out [rows][inter]. */
+int dcr_silu_mul_packed(const void* gate_up, int dtype, int rows, int inter, void* out,
+                        void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

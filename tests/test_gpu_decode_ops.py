@@ -1,5 +1,6 @@
 """The decode-step kernels around the attention (csrc/dcr_decode_ops.cu) against torch:
-residual add + HF LlamaRMSNorm, SiLU-gated product, and the skinny linear layer."""
+residual add + HF LlamaRMSNorm, the SiLU-gated product (plain and from packed gate/up
+weights), and the prologue reading q/k/v as strided slices of one packed GEMM output."""
 from __future__ import annotations
 
 import pytest
@@ -62,27 +63,42 @@ def test_silu_mul_matches_torch(dt):
     assert _ulps_apart(got, want).max().item() <= 1
 
 
-@pytest.mark.parametrize("M", [1, 4, 8])
-@pytest.mark.parametrize("N,K", [(2048, 2048), (8192, 2048), (2048, 8192), (77, 512)])
-def test_linear_skinny_matches_fp32_product(M, N, K):
-    from dcr_b200.kernel.cuda.decode_ops import linear_skinny
-    g = torch.Generator(device=DEV).manual_seed(3)
-    x = torch.randn(M, K, generator=g, device=DEV).to(torch.bfloat16)
-    w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).to(torch.bfloat16)
-    got = linear_skinny(x, w).float()
-    want = x.float() @ w.float().T
-    tol = 1e-2 * want.abs().max().item() + 1e-3
-    assert (got - want).abs().max().item() <= tol
-    assert torch.allclose(got, F.linear(x, w).float(), rtol=2e-2, atol=tol)
+def test_silu_mul_packed_and_packed_linears():
+    from dcr_b200.kernel.cuda.decode_ops import pack_linears, silu_mul_packed
+    g = torch.Generator(device=DEV).manual_seed(4)
+    gate = torch.nn.Linear(512, 1024, bias=False, device=DEV, dtype=torch.bfloat16)
+    up = torch.nn.Linear(512, 1024, bias=False, device=DEV, dtype=torch.bfloat16)
+    wg, wu = gate.weight.detach().clone(), up.weight.detach().clone()
+    packed = pack_linears(gate, up)
+    assert torch.equal(gate.weight, wg) and torch.equal(up.weight, wu)
+    assert gate.weight.data_ptr() == packed.data_ptr()
+    x = torch.randn(3, 512, generator=g, device=DEV).to(torch.bfloat16)
+    gu = F.linear(x, packed)
+    got = silu_mul_packed(gu)
+    want = F.silu(gu[:, :1024].contiguous()) * gu[:, 1024:].contiguous()
+    assert torch.equal(got, want) or _ulps_apart(got, want).max().item() <= 1
+    with torch.no_grad():
+        up.weight.mul_(2)   # writes land in the packed tensor
+    assert torch.equal(packed[1024:], 2 * wu)
 
 
-def test_linear_skinny_rejects_unsupported_shapes():
-    from dcr_b200 import _lib
-    from dcr_b200.kernel.cuda.decode_ops import linear_skinny
-    x = torch.randn(9, 512, device=DEV).to(torch.bfloat16)
-    w = torch.randn(64, 512, device=DEV).to(torch.bfloat16)
-    with pytest.raises(Exception):
-        linear_skinny(x, w)                      # 9 rows
-    lib = _lib.load()
-    assert lib.dcr_linear_skinny(x.data_ptr(), w.data_ptr(), 0, 4, 64, 300, x.data_ptr(),
-                                 None) == _lib.DCR_ERR_SHAPE  # K % 256 != 0
+def test_prologue_reads_packed_qkv_slices():
+    """append_rotated on q/k/v views into one [B, (H + 2 H_kv) D] GEMM output gives the
+    same cache rows and rotated query as on contiguous copies."""
+    from dcr_b200.kv_cache import StaticKVCache
+    from dcr_b200.models.llama.attention import llama3_inv_freq, rope_cos_sin
+    B, H, H_kv, D = 3, 8, 2, 64
+    g = torch.Generator(device=DEV).manual_seed(6)
+    qkv = torch.randn(B, (H + 2 * H_kv) * D, generator=g, device=DEV).to(torch.bfloat16)
+    q = qkv[:, :H * D].view(B, H, D)
+    k = qkv[:, H * D:(H + H_kv) * D].view(B, H_kv, D)
+    v = qkv[:, (H + H_kv) * D:].view(B, H_kv, D)
+    cos, sin = rope_cos_sin(torch.tensor([5, 6, 7], device=DEV), llama3_inv_freq().to(DEV),
+                            torch.bfloat16)
+    a = StaticKVCache(B, H_kv, 16, dtype=torch.bfloat16, device=DEV)
+    b = StaticKVCache(B, H_kv, 16, dtype=torch.bfloat16, device=DEV)
+    a.length = b.length = 4
+    qa, _ = a.append_rotated(q, k, v, cos, sin)
+    qb, _ = b.append_rotated(q.contiguous(), k.contiguous(), v.contiguous(), cos, sin)
+    assert torch.equal(qa, qb)
+    assert torch.equal(a.k[:, :, 4], b.k[:, :, 4]) and torch.equal(a.v[:, :, 4], b.v[:, :, 4])
