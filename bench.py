@@ -943,6 +943,81 @@ def run_sharded_arm(args):
     return 0
 
 
+def run_model_tp_arm(args):
+    """``--model-tp``: BASELINE config 4 end to end — greedy decode of the 16-layer
+    Llama-3.2-1B-architecture model (random-init bf16) with B=8, caches prefilled with
+    N=262144 synthetic positions, c=0.05, split by KV head over the N ranks (one GPU each,
+    two NCCL all-reduces per layer; N=1: the unsplit model). Each step is one CUDA graph
+    per rank (H2D tokens, 16 layers, LM head, argmax, D2H tokens) with a host sync; the
+    timed `model_steps` steps follow one untimed pass over the same steps; value = ms per
+    step, max over ranks. Prints one JSON line with its own metric."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200 import _lib
+    from dcr_b200.models.llama.model import (DCRLlamaDecoder, GreedyDecodeGraphs,
+                                              TPDCRLlamaDecoder)
+    rank, world, local = _env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    B, N0, c, steps = 8, 262144, 0.05, args.model_steps
+    kw = dict(attention="dcr", coverage_floor=c, dtype=torch.bfloat16, device=dev, seed=0)
+    model = (TPDCRLlamaDecoder(world=world, rank=rank, **kw) if world > 1
+             else DCRLlamaDecoder(**kw))
+    caches = model.new_caches(B, N0 + steps + 1)
+    model.prefill_synthetic(caches, N0, seed=100)
+    first = torch.randint(0, model.cfg.vocab, (B,), generator=torch.Generator().manual_seed(0))
+    out = {}
+    for name, attention in [("dcr_exact", "dcr"), ("dense_sdpa", "dense")]:
+        model.set_attention(attention)
+        for cc in caches:
+            cc.length = N0
+        runner = GreedyDecodeGraphs(model, caches, steps)
+        runner.run(first)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        a.record(runner.stream)
+        runner.run(first)
+        z.record(runner.stream)
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([a.elapsed_time(z) / steps], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = round(float(t), 4)
+        runner.close()
+        del runner
+    status = _lib.read_device_status(clear=True)
+    if rank == 0:
+        k = _k_eff(N0 + 1, c)
+        print(json.dumps({
+            "metric": "model decode ms/step (config4: 16 layers, B=8, N=262144, c=.05)",
+            "value": out["dcr_exact"], "unit": "ms/step", "n_gpus": world, "steps": steps,
+            "higher_is_better": False, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic (random-init weights, seeded caches)",
+            "config": {"workload": "config4 model decode", "B": B, "N": N0, "coverage": c,
+                       "k_eff_first_step": k, "layers": 16,
+                       "parallelism": f"KV heads split over {world} GPU(s), NCCL all-reduce "
+                                      f"after o_proj and down_proj" if world > 1
+                                      else "single GPU"},
+            "ms_per_step": out,
+            "api": "dcr_b200.models.llama.model.GreedyDecodeGraphs over "
+                   + ("TPDCRLlamaDecoder" if world > 1 else "DCRLlamaDecoder"),
+            "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+            "device_status": status}), flush=True)
+    del caches, model
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -955,6 +1030,8 @@ def main():
     ap.add_argument("--no-model", action="store_true",
                     help="skip the 16-layer model decode (config 2) measurement")
     ap.add_argument("--model-steps", type=int, default=64)
+    ap.add_argument("--model-tp", action="store_true",
+                    help="instead: config 4 model decode split by KV head over the ranks")
     ap.add_argument("--split", choices=["seq", "heads"], default="seq",
                     help="multi-GPU layout: context split by sequence (weak scaling, exact "
                          "global top-K) or KV heads split (strong scaling)")
@@ -968,6 +1045,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.model_tp:
+        return run_model_tp_arm(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         return run_sharded_arm(args)
     return run_gpu_arm(args)

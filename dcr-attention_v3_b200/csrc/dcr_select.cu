@@ -292,7 +292,14 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   int C = 1;
   while (C < kP2MaxCluster && static_cast<int64_t>(rows) * (2 * C) <= sms) C *= 2;
   while (C < kP2MaxCluster && nvec > C * kP2Threads * 8) C *= 2;
-  if (nvec > C * kP2Threads * 8) return DCR_ERR_SHAPE;  // more than 262144 positions per row
+  if (nvec > C * kP2Threads * 8) {
+    // past 262144 positions: 1024-thread CTAs with 40 keys per thread, up to 327680
+    int C2 = 1;
+    while (C2 < kP2MaxCluster && nvec > C2 * 1024 * 5) C2 *= 2;
+    if (nvec > C2 * 1024 * 5) return DCR_ERR_SHAPE;  // more than 327680 positions per row
+    p.seg_vec = (nvec + C2 - 1) / C2;
+    return launch_select_t<5, 1024>(p, rows, C2, st);
+  }
   p.seg_vec = (nvec + C - 1) / C;
 #if DCR_P2_WIDE
   // One CTA per row and every row on its own SM: 1024 threads with half the keys each

@@ -31,7 +31,8 @@ import torch.nn.functional as F
 
 from dcr_b200.kernel.cuda._common import HEAD_DIM, require
 from dcr_b200.kv_cache import StaticKVCache
-from dcr_b200.models.llama.attention import DCRDecodeAttention, llama3_inv_freq
+from dcr_b200.models.llama.attention import (DCRDecodeAttention, KVHeadParallelDecodeAttention,
+                                             llama3_inv_freq)
 
 
 @dataclass
@@ -118,9 +119,9 @@ class DCRLlamaDecoder(torch.nn.Module):
         self.T_dispatch = T_dispatch
         self.embed_tokens = torch.nn.Embedding(cfg.vocab, cfg.hidden, dtype=dtype, device=device)
         self.layers = torch.nn.ModuleList(
-            DecoderLayer(cfg, attention=attention, mode=mode, k_window=k_window,
-                         coverage_floor=coverage_floor, T_dispatch=T_dispatch, dtype=dtype,
-                         device=device, fast=fast)
+            self._make_layer(cfg, attention=attention, mode=mode, k_window=k_window,
+                             coverage_floor=coverage_floor, T_dispatch=T_dispatch, dtype=dtype,
+                             device=device, fast=fast)
             for _ in range(cfg.layers))
         self.norm = RMSNorm(cfg.hidden, cfg.rms_eps, dtype, device)
         self.inv_freq = llama3_inv_freq(HEAD_DIM, theta=cfg.rope_theta).to(self.device)
@@ -130,6 +131,9 @@ class DCRLlamaDecoder(torch.nn.Module):
                 if p.dim() == 2:
                     p.normal_(0.0, 0.02, generator=g)
         self.set_attention(attention)
+
+    def _make_layer(self, cfg, **kw) -> torch.nn.Module:
+        return DecoderLayer(cfg, **kw)
 
     def set_attention(self, attention: str) -> None:
         """'dcr': sparse step at or above T_dispatch positions; 'dense': SDPA everywhere."""
@@ -144,19 +148,30 @@ class DCRLlamaDecoder(torch.nn.Module):
     def new_caches(self, B: int, N_max: int, *, P: Optional[torch.Tensor] = None
                    ) -> List[StaticKVCache]:
         require(self.mode != "projected" or P is not None, "projected mode needs caches with P")
-        return [StaticKVCache(B, self.cfg.kv_heads, N_max, dtype=self.dtype, device=self.device,
-                              P=P) for _ in self.layers]
+        return [StaticKVCache(B, len(self.kv_heads_held()), N_max, dtype=self.dtype,
+                              device=self.device, P=P) for _ in self.layers]
+
+    def kv_heads_held(self) -> range:
+        """The global KV heads whose caches this model holds (all of them here)."""
+        return range(self.cfg.kv_heads)
 
     @torch.no_grad()
     def prefill_synthetic(self, caches: List[StaticKVCache], n: int, *, seed: int = 0) -> None:
         """Fills the first n positions of every layer's cache with seeded synthetic keys and
-        values (Q, K, V ~ N(0,1), keys of tokens 0-3 x4, two key channels x6) and their
-        projections; stands in for a prefill of real text."""
+        values (K, V ~ N(0,1), keys of tokens 0-3 x4, two key channels x6; one seed per
+        (layer, global KV head), so a head's rows do not depend on how the heads are split
+        across GPUs) and their projections; stands in for a prefill of real text."""
         from dcr_b200.synthetic import make_decode_inputs
+        heads = self.kv_heads_held()
         for i, cache in enumerate(caches):
             require(cache.length == 0, "prefill_synthetic expects empty caches")
-            _, K, V = make_decode_inputs(cache.B, self.cfg.kv_heads, self.cfg.kv_heads, n,
-                                         dtype=self.dtype, seed=seed + i, device=self.device)
+            require(cache.H_kv == len(heads), "cache heads do not match the model's")
+            K = torch.empty(cache.B, cache.H_kv, n, HEAD_DIM, dtype=self.dtype, device=self.device)
+            V = torch.empty_like(K)
+            for j, h in enumerate(heads):
+                _, K[:, j:j + 1], V[:, j:j + 1] = make_decode_inputs(
+                    cache.B, 1, 1, n, dtype=self.dtype, seed=seed + 1000 * i + h,
+                    device=self.device)
             cache.append(K, V)
             del K, V
 
@@ -184,6 +199,87 @@ class DCRLlamaDecoder(torch.nn.Module):
         else:
             x = self.norm(h + delta)
         return self.lm_head(x[:, 0])
+
+
+class TPDecoderLayer(DecoderLayer):
+    """The decoder layer split across the `world` ranks of a group (tensor parallelism by
+    KV head): the attention is :class:`KVHeadParallelDecodeAttention` (this rank's KV heads
+    and their query heads, a row-split o_proj and one all-reduce); the MLP holds columns
+    [r*I/W, (r+1)*I/W) of gate and up and the matching rows of down, whose partial output
+    is all-reduced. Norms and the residual stream are replicated."""
+
+    def __init__(self, cfg: LlamaDecodeConfig, *, world: int, rank: int, all_reduce,
+                 attention: str, mode: str, k_window: int, coverage_floor: float,
+                 T_dispatch: int, dtype, device, fast: bool):
+        require(fast, "the tensor-parallel layer runs the fused decode path")
+        require(cfg.intermediate % world == 0, "intermediate size must divide by the world")
+        torch.nn.Module.__init__(self)
+        kw = dict(bias=False, dtype=dtype, device=device)
+        self.fast = True
+        self.world, self.rank, self.all_reduce = world, rank, all_reduce
+        self.input_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps, dtype, device)
+        self.self_attn = KVHeadParallelDecodeAttention(
+            cfg.hidden, cfg.heads, cfg.kv_heads, world=world, rank=rank, all_reduce=all_reduce,
+            k_window=k_window, coverage_floor=coverage_floor,
+            T_dispatch=(1 << 62) if attention == "dense" else T_dispatch, mode=mode, dtype=dtype,
+            device=device, pack_qkv=True)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden, cfg.rms_eps, dtype, device)
+        inter = cfg.intermediate // world
+        self.gate_proj = torch.nn.Linear(cfg.hidden, inter, **kw)
+        self.up_proj = torch.nn.Linear(cfg.hidden, inter, **kw)
+        self.down_proj = torch.nn.Linear(inter, cfg.hidden, **kw)
+        from dcr_b200.kernel.cuda.decode_ops import pack_linears
+        self._gate_up = pack_linears(self.gate_proj, self.up_proj)
+
+    def forward(self, h, delta, cos, sin, cache):
+        h, d = super().forward(h, delta, cos, sin, cache)
+        if self.all_reduce is not None:
+            return h, self.all_reduce(d)
+        import torch.distributed as dist
+        dist.all_reduce(d, op=dist.ReduceOp.SUM)
+        return h, d
+
+    @torch.no_grad()
+    def load_shard(self, full: DecoderLayer) -> "TPDecoderLayer":
+        """Copies this rank's slices of an unsplit layer's weights."""
+        inter = self.gate_proj.weight.shape[0]
+        r = self.rank
+        self.input_layernorm.weight.copy_(full.input_layernorm.weight)
+        self.post_attention_layernorm.weight.copy_(full.post_attention_layernorm.weight)
+        self.self_attn.load_shard(full.self_attn)
+        self.gate_proj.weight.copy_(full.gate_proj.weight[r * inter:(r + 1) * inter])
+        self.up_proj.weight.copy_(full.up_proj.weight[r * inter:(r + 1) * inter])
+        self.down_proj.weight.copy_(full.down_proj.weight[:, r * inter:(r + 1) * inter])
+        return self
+
+
+class TPDCRLlamaDecoder(DCRLlamaDecoder):
+    """:class:`DCRLlamaDecoder` split across the ranks of a process group, one GPU each:
+    every layer is a :class:`TPDecoderLayer` (KV heads [r*H_kv/W, (r+1)*H_kv/W) and their
+    caches on rank r, two all-reduces per layer); the embedding, the norms and the tied LM
+    head are replicated, so every rank computes the same logits and greedy tokens.
+    ``all_reduce`` (optional) replaces torch.distributed's all-reduce (tests)."""
+
+    def __init__(self, cfg: Optional[LlamaDecodeConfig] = None, *, world: int, rank: int,
+                 all_reduce=None, **kw):
+        self.world, self.rank, self._ar = world, rank, all_reduce
+        super().__init__(cfg, **kw)
+
+    def _make_layer(self, cfg, **kw) -> torch.nn.Module:
+        return TPDecoderLayer(cfg, world=self.world, rank=self.rank, all_reduce=self._ar, **kw)
+
+    def kv_heads_held(self) -> range:
+        n = self.cfg.kv_heads // self.world
+        return range(self.rank * n, (self.rank + 1) * n)
+
+    @torch.no_grad()
+    def load_from(self, full: DCRLlamaDecoder) -> "TPDCRLlamaDecoder":
+        """Copies this rank's shard of an unsplit model's weights."""
+        self.embed_tokens.weight.copy_(full.embed_tokens.weight)
+        self.norm.weight.copy_(full.norm.weight)
+        for mine, theirs in zip(self.layers, full.layers):
+            mine.load_shard(theirs)
+        return self
 
 
 class GreedyDecodeGraphs:

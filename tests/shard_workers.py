@@ -122,3 +122,52 @@ def nccl_rank(rank: int, world: int, port: int, out_dir: str) -> None:
     torch.save(res, os.path.join(out_dir, f"rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()
+
+
+def tp_model_rank(rank: int, world: int, port: int, out_dir: str) -> None:
+    """A small Llama decode model split across `world` GPUs by KV head (TPDCRLlamaDecoder
+    over NCCL): one eager step's logits, the same model unsplit on every rank (its logits
+    for comparison), and 3 greedy steps replayed as per-step CUDA graphs holding the
+    all-reduces."""
+    _paths()
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200.models.llama.model import (DCRLlamaDecoder, GreedyDecodeGraphs,
+                                              LlamaDecodeConfig, TPDCRLlamaDecoder)
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=dev)
+    cfg = LlamaDecodeConfig(vocab=1000, hidden=512, intermediate=1024, layers=2, heads=8,
+                            kv_heads=2)
+    B, N0, steps = 2, 3000, 3
+    full = DCRLlamaDecoder(cfg, T_dispatch=1024, device=dev, seed=5)
+    tp = TPDCRLlamaDecoder(cfg, world=world, rank=rank, T_dispatch=1024, device=dev,
+                           seed=6).load_from(full)
+    cf = full.new_caches(B, N0 + steps + 1)
+    full.prefill_synthetic(cf, N0, seed=21)
+    ct = tp.new_caches(B, N0 + steps + 1)
+    tp.prefill_synthetic(ct, N0, seed=21)
+    cos, sin = full.rope_table(N0 + 1)
+    c1, s1 = cos[N0].expand(B, 64).contiguous(), sin[N0].expand(B, 64).contiguous()
+    tok = torch.tensor([4, 8], device=dev)
+    res = {"held": list(tp.kv_heads_held())}
+    for mode in ("dense", "dcr"):
+        full.set_attention(mode)
+        tp.set_attention(mode)
+        for c in cf + ct:
+            c.length = N0
+        res["full_" + mode] = full.step(tok, cf, c1, s1).float().cpu()
+        res["tp_" + mode] = tp.step(tok, ct, c1, s1).float().cpu()
+    for c in ct:
+        c.length = N0
+    runner = GreedyDecodeGraphs(tp, ct, steps)
+    res["tokens"] = runner.run(torch.tensor([4, 8]))
+    runner.close()
+    dist.barrier()
+    torch.save(res, os.path.join(out_dir, f"tp{rank}.pt"))
+    dist.destroy_process_group()

@@ -131,6 +131,7 @@ SWEEP = [
     (4, 32, 8, 32771, 4916, "bf16"),     # just past 32768: one 1024-thread CTA per row
     (4, 32, 8, 40960, 6144, "f16"),      # the longest row that shape covers
     (4, 32, 8, 40961, 6144, "bf16"),     # two-CTA clusters
+    (1, 4, 1, 262209, 13112, "bf16"),    # past 262144: 8-CTA clusters of 1024 threads
 ]
 
 

@@ -308,3 +308,37 @@ def test_two_gpus_nccl(oracle_mod, tmp_path):
     ok, st = attention_close(kv["O"].float().numpy(), kv["O_single"].float().numpy(),
                              got_rounded_to="bf16")
     assert ok, st
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_tensor_parallel_model_on_two_gpus(tmp_path):
+    """The Llama decode model split by KV head over 2 GPUs (two NCCL all-reduces per
+    layer) gives the unsplit model's logits within bf16 noise, the same logits and greedy
+    tokens on both ranks, and replays its steps as CUDA graphs holding the all-reduces."""
+    import shard_workers
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=shard_workers.tp_model_rank, args=(r, 2, port, str(tmp_path)))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = [torch.load(os.path.join(tmp_path, f"tp{r}.pt")) for r in range(2)]
+    assert res[0]["held"] == [0] and res[1]["held"] == [1]
+    assert torch.equal(res[0]["tokens"], res[1]["tokens"])
+    for mode in ("dense", "dcr"):
+        assert torch.equal(res[0]["tp_" + mode], res[1]["tp_" + mode])
+    # dense attention: only the rounding of the split GEMMs and the bf16 all-reduce differ
+    full, tp = res[0]["full_dense"], res[0]["tp_dense"]
+    assert (tp - full).abs().max().item() <= 3e-2 * max(full.abs().max().item(), 1.0)
+    # sparse: the same, plus top-K sets that may swap a near-tied boundary row when q and k
+    # differ in their last bits
+    full, tp = res[0]["full_dcr"], res[0]["tp_dcr"]
+    assert ((tp - full).norm() / full.norm()).item() <= 5e-2
