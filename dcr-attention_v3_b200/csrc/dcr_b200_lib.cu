@@ -11,3 +11,4 @@
 #include "dcr_capi.cu"
 #include "dcr_peer_capi.cu"
 #include "dcr_noalloc.cu"
+#include "dcr_runner.cu"

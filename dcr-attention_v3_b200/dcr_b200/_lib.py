@@ -73,6 +73,12 @@ SIGNATURES = {
     "dcr_decode_prologue_strided": (_i32, [_vp, _vp, _vp, _i64, _i64, _vp, _vp, _i32, _i32, _i32,
                                            _i32, _i32, _vp, _vp, _vp, _i64, _i64, _i32, _i32,
                                            _vp, _i32, _vp, _i64, _i64, _vp, _f32, _vp]),
+    "dcr_runner_create": (_i32, [_vp, _vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i64,
+                                 _i32, _i32, _i32, _i32, _i32, _i32, _f32, _vp]),
+    "dcr_runner_step": (_i32, [_vp, _vp, _vp]),
+    "dcr_runner_query_buffer": (_vp, [_vp]),
+    "dcr_runner_output_buffer": (_vp, [_vp]),
+    "dcr_runner_destroy": (_i32, [_vp]),
     "dcr_add_rmsnorm": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _f32, _vp, _vp, _vp]),
     "dcr_silu_mul": (_i32, [_vp, _vp, _i32, _i64, _vp, _vp]),
     "dcr_silu_mul_packed": (_i32, [_vp, _i32, _i32, _i32, _vp, _vp]),

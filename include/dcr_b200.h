@@ -348,6 +348,26 @@ int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int
  * Diagnostic: the reference has no counterpart (its kernels have no device status). */
 int dcr_read_device_status(int* status_out, int clear);
 
+/* ---- native step runner (dcr_runner.cu) ------------------------------------------
+ * One decode step over fixed caches — the H2D copy of the step's query from pinned
+ * staging, the three passes (dcr_decode, or dcr_decode_projected when KP and P are given)
+ * and the D2H copy of O — captured once as a CUDA graph on a runner-owned stream, with
+ * runner-owned device buffers, pinned staging and workspace. Replaces the per-step Python
+ * calls of the reference's hook (dcr_attention/models/llama/attention.py:805-813) for a
+ * serving loop; the graph bakes in the cache pointers, N and k_eff (one runner per length
+ * bucket). Create on the device that holds the caches (the current device). */
+int dcr_runner_create(const void* K, const void* V, const void* KP, const float* P, int dtype,
+                      int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                      int64_t v_stride_h, int64_t p_stride_b, int64_t p_stride_h, int B, int H,
+                      int H_kv, int N, int D, int k_eff, float eps, void** runner_out);
+/* Copies q_host [B, H, D] (host memory, the caches' dtype) into the staging, replays the
+ * step, waits for it and copies O [B, H, D] to o_host. Either pointer may be the runner's
+ * own pinned buffer (dcr_runner_query_buffer / dcr_runner_output_buffer): no copy then. */
+int dcr_runner_step(void* runner, const void* q_host, void* o_host);
+void* dcr_runner_query_buffer(void* runner);
+void* dcr_runner_output_buffer(void* runner);
+int dcr_runner_destroy(void* runner);
+
 /* ---- the rest of a decode step (dcr_decode_ops.cu) -----------------------------------
  * Kernels for the layers around the attention in a decode model (HF LlamaRMSNorm, the
  * residual adds, LlamaMLP's SiLU-gated product), with torch's rounding of the same op
