@@ -7,9 +7,9 @@
 // needed to produce that set in ascending order:
 //
 //   1. Map each bf16 score to an order-preserving 16-bit key (-0 -> +0, NaN -> top).
-//   2. Radix-select the k-th largest key T in two 8-bit levels: a 256-bin histogram of
-//      key >> 8 gives the high byte BH of T, then a 256-bin histogram of the low byte of
-//      the keys in BH gives T.
+//   2. Radix-select the k-th largest key T in two levels: a 4096-bin histogram of
+//      key >> 4 gives the high 12 bits BH of T, then a 16-bin histogram of the low 4 bits
+//      of the keys in BH gives T.
 //   3. need = k_eff - #{key > T}. Emit, in index order, every position with key > T and
 //      the first `need` positions with key == T. The output is the reference's set,
 //      already ascending.
@@ -18,8 +18,13 @@
 // rows, by a thread-block cluster of C CTAs (C = 1..8) that splits it into contiguous
 // segments. Each thread keeps a contiguous run of up to 64 keys in registers (loaded
 // once from L2, where Pass 1 just wrote them). Histograms are built with shared-memory
-// atomics and, in a cluster, added into CTA 0 through distributed shared memory; CTA 0's
-// bins are scanned by one warp. The per-CTA counts of keys > T and == T are exchanged
+// atomics and, in a cluster, added into CTA 0 through distributed shared memory; CTA 0
+// scans its 4096 bins block-wide and one warp scans the 16 low bins. The 12-bit first
+// level matters for decode scores: their keys crowd into a few exponents, so a 256-bin
+// first level leaves a quarter of the row in the threshold bin and every warp then issues
+// every second-level atomic; with 4096 bins the threshold bin holds a few percent of the
+// row and most warps skip most second-level atomics outright (a warp-uniform vote per key).
+// The per-CTA counts of keys > T and == T are exchanged
 // through CTA 0, and a block-wide exclusive scan of the packed per-thread counts gives
 // every thread its output offset and its rank among the equal keys. Threads emit their
 // selected positions from bit masks.
@@ -38,6 +43,8 @@ namespace dcr {
 constexpr int kP2Threads = 512;
 constexpr int kP2Warps = kP2Threads / 32;
 constexpr int kP2MaxCluster = 8;
+constexpr int kP2Bins1 = 4096;  // first level: key >> 4
+constexpr int kP2Bins2 = 16;    // second level: key & 15
 
 struct P2Params {
   const uint16_t* scores;
@@ -67,8 +74,9 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   constexpr int kWarpsB = TPB / 32;
   constexpr int kKeys = VPT * 8;
   constexpr int kWords = (kKeys + 31) / 32;
-  __shared__ uint32_t hist_hi[256];
-  __shared__ uint32_t hist_lo[256];
+  constexpr int kBpt = kP2Bins1 / TPB;  // first-level bins per thread in the search
+  __shared__ uint32_t hist_hi[kP2Bins1];
+  __shared__ uint32_t hist_lo[kP2Bins2];
   __shared__ uint32_t wsum[kWarpsB];
   __shared__ uint32_t scan_tot;
   __shared__ uint32_t cta_gt[kP2MaxCluster];
@@ -106,10 +114,13 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   };
 
   if (crank == 0 && tid == 0 && p.row_counters != nullptr) p.row_counters[row] = 0;
-  if (tid < 256) {
-    hist_lo[tid] = 0;
-    hist_hi[tid] = 0;
+  if (tid == 0) {
+    s_bh = 0;
+    s_above = 0;
   }
+#pragma unroll
+  for (int i = 0; i < kBpt; ++i) hist_hi[tid + i * TPB] = 0;
+  if (tid < kP2Bins2) hist_lo[tid] = 0;
 
   // ---- keys of this thread: positions [v0 * 8, (v0 + VPT) * 8), 0 past the segment ----
   // Key 0 ranks below every real score (the smallest real key, -inf's, is 0x007f), so
@@ -144,34 +155,64 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   }
   row_sync();  // histograms initialised everywhere before anyone adds into CTA 0's
 
-  // ---- level 1: histogram of the high byte, added into CTA 0 -------------------------
+  // ---- level 1: histogram of the high 12 bits, added into CTA 0 -----------------------
 #pragma unroll
   for (int e = 0; e < kKeys; ++e)
-    if (key[e] != 0u) atomicAdd(&hist_hi[key[e] >> 8], 1u);
+    if (key[e] != 0u) atomicAdd(&hist_hi[key[e] >> 4], 1u);
   if (C > 1) {
     __syncthreads();
-    if (crank != 0 && tid < 256 && hist_hi[tid]) atomicAdd(hist_hi0 + tid, hist_hi[tid]);
+    if (crank != 0) {
+#pragma unroll
+      for (int i = 0; i < kBpt; ++i) {
+        const uint32_t c = hist_hi[tid + i * TPB];
+        if (c) atomicAdd(hist_hi0 + tid + i * TPB, c);
+      }
+    }
   }
   row_sync();
-  if (crank == 0 && warp == 0) {
-    int bin;
-    uint32_t above;
-    warp_find_bin(hist_hi, static_cast<uint32_t>(k), bin, above);
-    if (lane == 0) {
-      s_bh = bin;
-      s_above = above;
+  if (crank == 0) {
+    // block-wide search from the top: thread t holds bins [kBpt g, kBpt g + kBpt) with
+    // g = TPB - 1 - t, so thread 0 holds the highest bins
+    const int g = TPB - 1 - tid;
+    uint32_t c[kBpt], tot = 0;
+#pragma unroll
+    for (int i = 0; i < kBpt; ++i) {
+      c[i] = hist_hi[kBpt * g + i];
+      tot += c[i];
+    }
+    const uint32_t incl = warp_incl_scan(tot);
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const uint32_t ws = lane < kWarpsB ? wsum[lane] : 0u;
+      const uint32_t wi = warp_incl_scan(ws);
+      if (lane < kWarpsB) wsum[lane] = wi - ws;
+    }
+    __syncthreads();
+    uint32_t a = incl - tot + wsum[warp];  // keys in the bins above this thread's
+#pragma unroll
+    for (int i = kBpt - 1; i >= 0; --i) {
+      if (a < static_cast<uint32_t>(k) && static_cast<uint32_t>(k) <= a + c[i]) {
+        s_bh = kBpt * g + i;
+        s_above = a;
+      }
+      a += c[i];
     }
   }
   row_sync();
   const uint32_t bh = static_cast<uint32_t>(*bh0);
 
-  // ---- level 2: low byte of the keys in BH --------------------------------------------
+  // ---- level 2: low 4 bits of the keys in BH (a warp skips a key no lane has in BH) ---
 #pragma unroll
-  for (int e = 0; e < kKeys; ++e)
-    if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist_lo[key[e] & 0xffu], 1u);
+  for (int e = 0; e < kKeys; ++e) {
+    const bool in_bh = (key[e] >> 4) == bh && key[e] != 0u;
+    if (__any_sync(0xffffffffu, in_bh)) {
+      if (in_bh) atomicAdd(&hist_lo[key[e] & 15u], 1u);
+    }
+  }
   if (C > 1) {
     __syncthreads();
-    if (crank != 0 && tid < 256 && hist_lo[tid]) atomicAdd(hist_lo0 + tid, hist_lo[tid]);
+    if (crank != 0 && tid < kP2Bins2 && hist_lo[tid]) atomicAdd(hist_lo0 + tid, hist_lo[tid]);
   }
   row_sync();
 
@@ -179,12 +220,20 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   __shared__ uint32_t s_T;
   __shared__ int s_need;
   if (warp == 0) {
-    int lo;
-    uint32_t above_lo;
-    warp_find_bin(hist_lo0, static_cast<uint32_t>(k) - *above0, lo, above_lo);
-    if (lane == 0) {
-      s_T = (bh << 8) | static_cast<uint32_t>(lo);
-      s_need = k - static_cast<int>(*above0 + above_lo);  // minus #{key > T}
+    // lane l < 16 holds low bin 15 - l (lane 0 the highest)
+    const uint32_t above = *above0;
+    const uint32_t kk = static_cast<uint32_t>(k) - above;
+    const uint32_t c = lane < kP2Bins2 ? hist_lo0[kP2Bins2 - 1 - lane] : 0u;
+    const uint32_t incl = warp_incl_scan(c);
+    const bool hit = lane < kP2Bins2 && incl - c < kk && kk <= incl;
+    const uint32_t m = __ballot_sync(0xffffffffu, hit);
+    if (m != 0u && lane == __ffs(m) - 1) {
+      s_T = (bh << 4) | static_cast<uint32_t>(kP2Bins2 - 1 - lane);
+      s_need = k - static_cast<int>(above + (incl - c));  // minus #{key > T}
+    } else if (m == 0u && lane == 0) {  // inconsistent counts: select nothing, report
+      s_T = 0x10000u;
+      s_need = 0;
+      raise_status(DCR_ERR_DEVICE_INDEX);
     }
   }
   __syncthreads();

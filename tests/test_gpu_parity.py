@@ -239,6 +239,53 @@ def test_errors_mirror_reference():
         _api().topk_qaxis_attention(Q.cpu(), K.cpu(), V.cpu(), 4)
 
 
+def _stable_topk_reference(scores: torch.Tensor, k: int) -> torch.Tensor:
+    """The reference's selection restated with torch: order keys of the bf16 bits (-0 as +0,
+    every NaN on top), a stable descending sort, the first k positions, ascending."""
+    x = scores.contiguous().view(torch.int16).to(torch.int32) & 0xFFFF
+    mag = x & 0x7FFF
+    x = torch.where(mag == 0, torch.zeros_like(x), x)
+    key = x ^ (((x >> 15) * 0x7FFF) | 0x8000)
+    key = torch.where(mag > 0x7F80, torch.full_like(key, 0xFFFF), key)
+    order = torch.sort(-key.to(torch.int64), dim=-1, stable=True).indices
+    return torch.sort(order[..., :k], dim=-1).values.to(torch.int32)
+
+
+def _adversarial_rows(kind: str, R: int, N: int, g: torch.Generator) -> torch.Tensor:
+    if kind == "all_equal":
+        s = torch.full((R, N), 0.75)
+    elif kind == "three_values":
+        s = torch.tensor([-1.0, 0.5, 2.0])[torch.randint(0, 3, (R, N), generator=g)]
+    elif kind == "narrow":  # one exponent: every key shares the top 8 bits
+        s = 1.0 + torch.rand(R, N, generator=g)
+    elif kind == "raw_bits":  # every bf16 pattern: NaNs, +-inf, -0/+0, subnormals
+        bits = torch.randint(0, 1 << 16, (R, N), generator=g, dtype=torch.int32)
+        return (bits - ((bits >= 1 << 15).to(torch.int32) << 16)).to(torch.int16).view(
+            torch.bfloat16)
+    elif kind == "specials":
+        vals = torch.tensor([float("nan"), float("inf"), -float("inf"), 0.0, -0.0, 1.0, -1.0])
+        s = vals[torch.randint(0, len(vals), (R, N), generator=g)]
+    else:  # decode-like: N(0, 1.45^2), the bench's score spread
+        s = torch.randn(R, N, generator=g) * 1.45
+    return s.to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("kind,R,N,k", [
+    ("all_equal", 4, 1000, 300), ("three_values", 8, 40000, 17000), ("narrow", 8, 32768, 4916),
+    ("raw_bits", 8, 5000, 2500), ("specials", 4, 3001, 1500), ("decode", 128, 32768, 4916),
+    ("decode", 4, 32768, 1), ("decode", 4, 32768, 32767), ("three_values", 2, 70000, 30001),
+    ("decode", 1, 300000, 45000), ("narrow", 2, 262209, 39331), ("raw_bits", 3, 65536, 9830),
+])
+def test_pass2_adversarial_distributions(kind, R, N, k):
+    """Pass 2 on score rows built to stress the radix select (ties across and inside the
+    threshold bin, every bf16 pattern, k = 1 and k = N, one- and multi-CTA rows) against
+    a stable torch sort of the same order keys: bit-exact."""
+    g = torch.Generator().manual_seed(sum(map(ord, kind)) * 7919 + R * 131 + N + k)
+    scores = _adversarial_rows(kind, R, N, g).reshape(1, R, N).to(DEV)
+    idx = _api().topk_pass2_select(scores, k)
+    assert torch.equal(idx, _stable_topk_reference(scores, k))
+
+
 # ---------------------------------------------------------------------------------------
 # Full size: BASELINE config 1 (hero), config 3 corners, one GPU's shard of config 4
 # ---------------------------------------------------------------------------------------
