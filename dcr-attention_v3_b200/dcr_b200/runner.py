@@ -7,7 +7,9 @@ step for a serving loop that keeps its caches in place, on the library's native 
 (dcr_runner_create / dcr_runner_step): the copy of the step's query from pinned staging,
 the three passes and the copy of O back are captured once into a CUDA graph, and a step is
 one C call — a host copy into the staging, one graph launch, one synchronisation, a host
-copy out. The graph bakes in the cache tensors and the context length N: keep a runner per
+copy out. Inside the graph two small kernels move Q from the pinned staging to the device
+and O back, reading and writing the mapped host buffers over the bus: copy-engine nodes
+cost several microseconds each to start, a 16 KB kernel copy about one. The graph bakes in the cache tensors and the context length N: keep a runner per
 length bucket (or make a new one when N changes).
 """
 from __future__ import annotations
@@ -45,9 +47,10 @@ class DecodeRunner:
             psb, psh = kp_strides(KP)
         self.device = K_cache.device
         self.dtype = K_cache.dtype
-        self.shape = (B, H, HEAD_DIM)
+        self.shape = torch.Size((B, H, HEAD_DIM))
         self._keep = (K_cache, V_cache, KP, P)  # the graph reads these buffers
         self._lib = _lib.load()
+        self._step = self._lib.dcr_runner_step
         handle = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             st = self._lib.dcr_runner_create(
@@ -70,18 +73,24 @@ class DecodeRunner:
         """Runs one step for the host query q [B, H, D]; returns O [B, H, D] on the host
         (``out`` if given, else a view of the runner's pinned buffer, valid until the next
         call)."""
-        require(self._h is not None, "runner is closed")
-        require(tuple(q.shape) == self.shape and q.dtype == self.dtype and not q.is_cuda and
-                q.is_contiguous(), f"q must be a contiguous host {self.dtype} {self.shape}")
+        # the checks run on every step, so their messages are only formatted on failure
+        if self._h is None:
+            raise AssertionError("runner is closed")
+        if not self._host_ok(q):
+            raise AssertionError(f"q must be a contiguous host {self.dtype} {self.shape}")
         dst = self.o_host
         if out is not None:
-            require(tuple(out.shape) == self.shape and out.dtype == self.dtype and
-                    not out.is_cuda and out.is_contiguous(),
-                    f"out must be a contiguous host {self.dtype} {self.shape}")
+            if not self._host_ok(out):
+                raise AssertionError(f"out must be a contiguous host {self.dtype} {self.shape}")
             dst = out
-        st = self._lib.dcr_runner_step(self._h, q.data_ptr(), dst.data_ptr())
-        _lib.check(st, "dcr_runner_step")
+        st = self._step(self._h, q.data_ptr(), dst.data_ptr())
+        if st != 0:
+            _lib.check(st, "dcr_runner_step")
         return dst
+
+    def _host_ok(self, t: torch.Tensor) -> bool:
+        return (t.shape == self.shape and t.dtype == self.dtype and not t.is_cuda and
+                t.is_contiguous())
 
     def close(self) -> None:
         """Frees the runner (graph, stream, buffers); its pinned-buffer views die with it."""
