@@ -259,26 +259,52 @@ int launch_append(const void* k_new, const void* v_new, int64_t nsb, int64_t nsh
   }
 }
 
-template <typename T>
-static int launch_score_proj_t(ProjScoreParams p, int B, int G, cudaStream_t st) {
-  // one wave: about 5 CTAs per SM (the register limit of the 16-bit G = 4 case) spread over the (b, h_kv) groups, each CTA looping over
-  // its group's tiles (the unit queries and projections are computed once per CTA)
+// Resident CTAs per SM of one instantiation (registers decide it: 102 for the 16-bit G = 4
+// kernel, which rounds to 4 CTAs of 128 threads per SM).
+template <typename T, int G>
+static int score_proj_ctas_per_sm() {
+  static int n = 0;
+  if (n == 0) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, score_proj_kernel<T, G>, kSpThreads, 0) !=
+            cudaSuccess ||
+        v < 1)
+      v = 1;
+    n = v;
+  }
+  return n;
+}
+
+template <typename T, int G>
+static int launch_score_proj_tg(ProjScoreParams p, int B, cudaStream_t st) {
+  // One wave spread over the (b, h_kv) groups, each CTA looping over its group's tiles (the
+  // unit queries and projections are computed once per CTA). The CTAs per group are the
+  // fewest that keep the longest CTA at ceil(tiles / (slots per group)) tiles, so a group's
+  // CTAs take equal shares and the grid never spills into a second wave (sized for 5 CTAs
+  // per SM where registers allow 4, the hero grid ran 768 CTAs on 592 slots).
   const int64_t groups = static_cast<int64_t>(B) * p.H_kv;
-  int64_t cpg = (static_cast<int64_t>(device_sm_count()) * 5 + groups - 1) / groups;
+  const int64_t slots = static_cast<int64_t>(device_sm_count()) * score_proj_ctas_per_sm<T, G>();
+  int64_t cpg = slots / groups;
   if (cpg > p.tiles) cpg = p.tiles;
   if (cpg < 1) cpg = 1;
+  const int64_t per_cta = (p.tiles + cpg - 1) / cpg;
+  cpg = (p.tiles + per_cta - 1) / per_cta;
   p.cpg = static_cast<int>(cpg);
   const int64_t blocks = groups * cpg;
   if (blocks > 0x7fffffff) return DCR_ERR_SHAPE;
-  const unsigned nb = static_cast<unsigned>(blocks);
+  score_proj_kernel<T, G><<<static_cast<unsigned>(blocks), kSpThreads, 0, st>>>(p);
+  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+}
+
+template <typename T>
+static int launch_score_proj_t(ProjScoreParams p, int B, int G, cudaStream_t st) {
   switch (G) {
-    case 1: score_proj_kernel<T, 1><<<nb, kSpThreads, 0, st>>>(p); break;
-    case 2: score_proj_kernel<T, 2><<<nb, kSpThreads, 0, st>>>(p); break;
-    case 4: score_proj_kernel<T, 4><<<nb, kSpThreads, 0, st>>>(p); break;
-    case 8: score_proj_kernel<T, 8><<<nb, kSpThreads, 0, st>>>(p); break;
+    case 1: return launch_score_proj_tg<T, 1>(p, B, st);
+    case 2: return launch_score_proj_tg<T, 2>(p, B, st);
+    case 4: return launch_score_proj_tg<T, 4>(p, B, st);
+    case 8: return launch_score_proj_tg<T, 8>(p, B, st);
     default: return DCR_ERR_SHAPE;
   }
-  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }
 
 int launch_score_projected(const void* KP, int dtype, int64_t p_stride_b, int64_t p_stride_h,

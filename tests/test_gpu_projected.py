@@ -52,7 +52,8 @@ def test_project_keys_strided_cache_view(oracle_mod, cuda_lib):
 
 @pytest.mark.parametrize("dt", DTS)
 @pytest.mark.parametrize("B,H,H_kv,N,k", [(1, 32, 8, 4096, 614), (2, 16, 2, 2001, 300),
-                                          (3, 8, 8, 517, 78), (1, 64, 8, 3000, 450)])
+                                          (3, 8, 8, 517, 78), (1, 64, 8, 3000, 450),
+                                          (2, 8, 4, 9000, 1200)])
 def test_projected_select_and_decode_vs_oracle(oracle_mod, cuda_lib, dt, B, H, H_kv, N, k):
     from dcr_b200 import _lib
     from dcr_b200.kernel.cuda import (project_keys, topk_qaxis_attention_projected,
@@ -80,6 +81,36 @@ def test_projected_select_and_decode_vs_oracle(oracle_mod, cuda_lib, dt, B, H, H
     assert _lib.read_device_status(clear=True) == 0
     ok, stats = attention_close(O.float().cpu().numpy(), O_ref, got_rounded_to=n)
     assert ok, stats
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_projected_scores_reject_unaligned_kp(cuda_lib, dt):
+    """Projected Pass 1 reads KP rows with 16-byte vector loads: a KP view that does not
+    start on a 16-byte boundary is refused with DCR_ERR_ALIGN, and the same rows copied to
+    an aligned buffer score normally."""
+    from dcr_b200 import _lib
+    from dcr_b200.kernel.cuda import project_keys
+    from dcr_b200.synthetic import make_decode_inputs
+    B, H, H_kv, N = 2, 16, 4, 3001
+    Q, K, _ = make_decode_inputs(B, H, H_kv, N, dtype=dt, seed=17, device=DEV)
+    Pd = _P().to(DEV)
+    KP = project_keys(K, Pd)
+    esz = KP.element_size()
+    flat = torch.empty(KP.numel() + 16 // esz, dtype=dt, device=DEV)
+    off = 8 // esz
+    KPu = flat[off:off + KP.numel()].view(KP.shape)
+    KPu.copy_(KP)
+    assert KPu.data_ptr() % 16 == 8
+
+    def score(kp):
+        out = torch.empty(B * H, N, dtype=torch.int16, device=DEV)
+        return cuda_lib.dcr_score_projected(kp.data_ptr(), _lib.DTYPE_CODES[dt], kp.stride(0),
+                                            kp.stride(1), Q.data_ptr(), 1e-12, Pd.data_ptr(),
+                                            16, None, B, H, H_kv, N, 64, out.data_ptr(), N, None)
+
+    assert score(KPu) == _lib.DCR_ERR_ALIGN
+    assert score(KP) == 0
+    assert _lib.read_device_status(clear=True) == 0
 
 
 @pytest.mark.slow
