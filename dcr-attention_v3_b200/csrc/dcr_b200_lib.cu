@@ -4,6 +4,7 @@
 #include "dcr_score.cu"
 #include "dcr_select.cu"
 #include "dcr_attend.cu"
+#include "dcr_attend_union.cu"
 #include "dcr_shard.cu"
 #include "dcr_project.cu"
 #include "dcr_rope.cu"

@@ -51,16 +51,24 @@ static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 WorkspaceLayout workspace_layout(int rows, int N, int k_eff) {
   WorkspaceLayout w;
   w.splits = attend_splits(rows, k_eff);
+  w.part_splits = w.splits;
+  if (union_enabled() && union_max_splits(N) > w.part_splits) w.part_splits = union_max_splits(N);
   w.n_pad = (static_cast<int64_t>(N) + 7) / 8 * 8;
   size_t off = 0;
   w.counters = off;
   off = align_up(off + sizeof(int) * static_cast<size_t>(rows), 256);
   w.partials = off;
-  off = align_up(off + sizeof(float) * static_cast<size_t>(rows) * w.splits * (kD + 2), 256);
+  off = align_up(off + sizeof(float) * static_cast<size_t>(rows) * w.part_splits * (kD + 2), 256);
   w.scores = off;
   off = align_up(off + sizeof(uint16_t) * static_cast<size_t>(rows) * w.n_pad, 256);
   w.idx = off;
   off = align_up(off + sizeof(int32_t) * static_cast<size_t>(rows) * k_eff, 256);
+  w.bits = off;
+  w.bits_stride = 0;
+  if (union_enabled()) {
+    w.bits_stride = (static_cast<int64_t>(N) + 31) / 32;
+    off = align_up(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.bits_stride, 256);
+  }
   w.total = off;
   return w;
 }
@@ -308,8 +316,21 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   if (st) return st;
   if ((st = mark(1))) return st;
   // Pass 2 also resets the Pass 3 split-K tickets of its row.
-  if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s))) return st;
+  // With the union Pass 3, Pass 2 writes selection bitmaps where its layout allows.
+  const bool use_union = union_enabled() && union_supported(dtype, H, H_kv);
+  uint32_t* bits = reinterpret_cast<uint32_t*>(ws + w.bits);
+  int bits_written = 0;
+  if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s,
+                          use_union ? bits : nullptr, w.bits_stride, &bits_written)))
+    return st;
   if ((st = mark(2))) return st;
+  if (union_enabled() && union_supported(dtype, H, H_kv)) {
+    if ((st = launch_attend_union(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+                                  idx, bits_written ? bits : nullptr, w.bits_stride, B, H, H_kv,
+                                  N, k_eff, O, partials, w.part_splits, counters, s)))
+      return st;
+    return mark(3);
+  }
   if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, idx,
                           nullptr, B, H, H_kv, N, k_eff, O, nullptr, w.splits, partials,
                           counters, nullptr, s)))

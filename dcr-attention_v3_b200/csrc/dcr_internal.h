@@ -54,14 +54,29 @@ cudaError_t launch_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem, cu
 // Split-K factor used by Pass 3 for this shape (1 = no split, no workspace partials).
 int attend_splits(int rows, int k_eff);
 
+// Union Pass 3 (dcr_attend_union.cu): positions per CTA range at most kUnSpanMax; the
+// workspace partials hold union_max_splits(N) splits per row.
+constexpr int kUnSpanMax = 4096;
+int union_max_splits(int N);
+bool union_supported(int dtype, int H, int H_kv);
+bool union_enabled();
+int launch_attend_union(const void* Q, const void* K, const void* V, int dtype, int64_t ksb,
+                        int64_t ksh, int64_t vsb, int64_t vsh, const int32_t* idx,
+                        const uint32_t* bits, int64_t bits_stride, int B, int H, int H_kv, int N,
+                        int k_eff, void* O, float* partials, int part_splits, int* counters,
+                        cudaStream_t st);
+
 // Workspace layout shared by dcr_decode / dcr_select_indices / dcr_attend.
 struct WorkspaceLayout {
   size_t counters;  // int32 [rows]
   size_t partials;  // fp32 [rows * splits * (D + 2)]
   size_t scores;    // uint16 [rows * n_pad]
   size_t idx;       // int32 [rows * k_eff]
+  size_t bits;      // uint32 [rows * bits_stride] selection bitmaps (union Pass 3 only)
+  int64_t bits_stride;
   size_t total;
   int splits;
+  int part_splits;  // splits the partials hold (>= splits; the union Pass 3 may use more)
   int64_t n_pad;
 };
 WorkspaceLayout workspace_layout(int rows, int N, int k_eff);
@@ -74,8 +89,12 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
                  uint16_t* scores, int64_t s_stride_row, int keys_out, cudaStream_t st);
 
 // keys_in != 0: the rows hold order keys (from launch_score with keys_out) not bf16 bits.
+// bits (optional): when every thread's positions are whole 32-bit words of the row, the
+// selection is written as a bitmap [rows][bits_stride] words (bit n of word n / 32) instead
+// of the index lists, and *bits_written is set to 1; otherwise idx is written and it is 0.
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
-                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st);
+                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st,
+                  uint32_t* bits = nullptr, int64_t bits_stride = 0, int* bits_written = nullptr);
 
 // counts (optional): row r attends to the first counts[r] of its k_eff index slots.
 // state (optional): write the unnormalised (m, l, o[D]) per row (m in base-2 units of

@@ -56,6 +56,8 @@ struct P2Params {
   int vec;                // rows are 16-byte aligned: 8 keys per uint4 load
   int keys_in;            // rows already hold order keys (Pass 1 keys_out), not bf16 bits
   int seg_vec;            // vectors (8 positions) per CTA segment
+  uint32_t* bits;         // optional bitmap output instead of idx (whole-word layouts only)
+  int64_t bits_stride;    // words per bitmap row
 };
 
 // Branch-free order key of a raw bf16 score (same map as bf16_order_key): -0 and +0
@@ -288,8 +290,32 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   const int eq_before = static_cast<int>(eq_before_cta + (ex >> 16));
   int pos = static_cast<int>(gt_before + (ex & 0xffffu)) + min(eq_before, need);
   int take = need - eq_before;  // ties this thread may take, lowest positions first
-  int32_t* out = p.idx + static_cast<int64_t>(row) * k;
   const int base = v0 * 8;
+  if (p.bits != nullptr) {
+    // whole words: base is a multiple of 32 (VPT % 4 == 0, segments word-aligned); a word
+    // is written by the thread whose positions start it, if it starts inside the segment
+    uint32_t* brow = p.bits + static_cast<int64_t>(row) * p.bits_stride;
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+      uint32_t sel = gtm[w];
+      const uint32_t eq = eqm[w];
+      const int neq_w = __popc(eq);
+      if (take >= neq_w) {
+        sel |= eq;
+        take -= neq_w;
+      } else if (take > 0) {
+        uint32_t rem = eq;
+        for (int i = 0; i < take; ++i) rem &= rem - 1;
+        sel |= eq & ~rem;
+        take = 0;
+      }
+      const int start = base + 32 * w;
+      if (start < v_end * 8 && start < N) brow[start >> 5] = sel;
+    }
+    if (C > 1) cluster.sync();
+    return;
+  }
+  int32_t* out = p.idx + static_cast<int64_t>(row) * k;
 #pragma unroll
   for (int w = 0; w < kWords; ++w) {
     uint32_t sel = gtm[w];
@@ -324,8 +350,20 @@ static int launch_select_t(const P2Params& p, int rows, int C, cudaStream_t st) 
 }
 
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
-                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st) {
+                  int keys_in, int32_t* idx, int* row_counters, cudaStream_t st, uint32_t* bits,
+                  int64_t bits_stride, int* bits_written) {
+  if (bits_written != nullptr) *bits_written = 0;
+  // the bitmap goes out only where every thread's keys are whole aligned words
+  auto with_bits = [&](P2Params& q, int vpt, int C) {
+    if (bits != nullptr && vpt % 4 == 0 && (C == 1 || q.seg_vec % 4 == 0)) {
+      q.bits = bits;
+      q.bits_stride = bits_stride;
+      if (bits_written != nullptr) *bits_written = 1;
+    }
+  };
   P2Params p;
+  p.bits = nullptr;
+  p.bits_stride = 0;
   p.scores = scores;
   p.stride = s_stride_row;
   p.N = N;
@@ -347,14 +385,16 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
     while (C2 < kP2MaxCluster && nvec > C2 * 1024 * 5) C2 *= 2;
     if (nvec > C2 * 1024 * 5) return DCR_ERR_SHAPE;  // more than 327680 positions per row
     p.seg_vec = (nvec + C2 - 1) / C2;
-    return launch_select_t<5, 1024>(p, rows, C2, st);
+    return launch_select_t<5, 1024>(p, rows, C2, st);  // 40 keys per thread: no bitmap
   }
   p.seg_vec = (nvec + C - 1) / C;
 #if DCR_P2_WIDE
   // One CTA per row and every row on its own SM: 1024 threads with half the keys each
   // (up to 32 per thread, which fit the 64 registers a 1024-thread CTA allows).
-  if (C == 1 && rows <= sms && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4)
+  if (C == 1 && rows <= sms && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4) {
+    with_bits(p, 4, C);
     return launch_select_t<4, 1024>(p, rows, C, st);
+  }
   // Just past 32768 positions a two-CTA cluster per row would need two waves for 128
   // rows: one 1024-thread CTA with 40 keys per thread covers up to 40960 positions.
   if (rows <= sms && nvec > 1024 * 4 && nvec <= 1024 * 5) {
@@ -365,7 +405,11 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   const int vpt = (p.seg_vec + kP2Threads - 1) / kP2Threads;
   if (vpt <= 1) return launch_select_t<1, kP2Threads>(p, rows, C, st);
   if (vpt <= 2) return launch_select_t<2, kP2Threads>(p, rows, C, st);
-  if (vpt <= 4) return launch_select_t<4, kP2Threads>(p, rows, C, st);
+  if (vpt <= 4) {
+    with_bits(p, 4, C);
+    return launch_select_t<4, kP2Threads>(p, rows, C, st);
+  }
+  with_bits(p, 8, C);
   return launch_select_t<8, kP2Threads>(p, rows, C, st);
 }
 
