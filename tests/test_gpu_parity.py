@@ -153,6 +153,49 @@ def test_sweep_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
     _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
 
 
+@pytest.mark.parametrize("B,H,H_kv,N,k,dt", [
+    (1, 32, 8, 65536, 9830, "bf16"),   # Pass 2 in clusters of 4 CTAs: bitmaps per segment
+    (8, 32, 8, 16384, 2457, "f16"),    # more rows than SMs
+    (2, 16, 2, 2001, 300, "bf16"),     # G = 8, index lists searched (no bitmaps)
+])
+def test_union_pass3_shapes_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
+    """The decode step's Pass 3 over each KV head's union of selections (bitmaps from Pass 2,
+    or the heads' index lists where Pass 2 cannot write whole words) against the oracle."""
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=DT[dt], seed=N + k + 1)
+    _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
+
+
+def test_union_pass3_keeps_nonfinite_v_rows_to_their_heads(oracle_mod):
+    """A V row holding inf or NaN that only one head of a KV group selected reaches that
+    head's output and no other (the union kernel scores every union row for all heads, so
+    the rows a head did not select must not be multiplied in, not even by a weight of 0)."""
+    from dcr_b200.synthetic import make_decode_inputs
+    B, H, H_kv, N, k = 2, 32, 8, 5000, 750
+    G = H // H_kv
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.float16, seed=21)
+    idx = _api().topk_qaxis_select(Q.to(DEV), K.to(DEV), k).cpu()
+    planted = 0
+    for b in range(B):
+        for hk in range(H_kv):
+            sel = [set(idx[b, hk * G + j].tolist()) for j in range(G)]
+            only0 = sorted(sel[0] - set().union(*sel[1:]))
+            if only0:
+                V[b, hk, only0[0], 3] = float("inf")
+                V[b, hk, only0[-1], 60] = float("nan")
+                planted += 1
+    assert planted > 0
+    O = _api().topk_qaxis_attention(Q.to(DEV), K.to(DEV), V.to(DEV), k).float().cpu()
+    _, _, _, O_o = oracle_mod.decode(to_np(Q), to_np(K), to_np(V), "f16", k)
+    O_o = torch.from_numpy(np.asarray(O_o, dtype=np.float32)).reshape(O.shape)
+    assert torch.equal(torch.isfinite(O), torch.isfinite(O_o))
+    rows = torch.isfinite(O_o.reshape(-1, 64)).all(-1)
+    assert 0 < int((~rows).sum()) < rows.numel()
+    ok, st = attention_close(O.reshape(-1, 64)[rows].numpy(), O_o.reshape(-1, 64)[rows].numpy(),
+                             got_rounded_to="f16")
+    assert ok, st
+
+
 def test_strided_cache_view_matches_contiguous(oracle_mod):
     """A cache allocated for N_max positions is used through a view, without a copy."""
     from dcr_b200.synthetic import make_decode_inputs
