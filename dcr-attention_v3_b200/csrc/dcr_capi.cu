@@ -283,7 +283,8 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
                        int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
                        int64_t v_stride_h, int B, int H, int H_kv, int N, int D, int k_eff,
                        float eps, void* O, void* workspace, size_t workspace_bytes,
-                       void* stream, void* const* events, const ProjArgs* proj = nullptr) {
+                       void* stream, void* const* events, const ProjArgs* proj = nullptr,
+                       int passes = 3) {
   int st = check_heads(B, H, H_kv, N, D);
   if (st) return st;
   if ((st = check_cache(K, dtype, k_stride_b, k_stride_h, B, H_kv, N))) return st;
@@ -315,6 +316,7 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
                       w.n_pad, 1, s);
   if (st) return st;
   if ((st = mark(1))) return st;
+  if (passes < 2) return DCR_OK;
   // Pass 2 also resets the Pass 3 split-K tickets of its row.
   // With the union Pass 3, Pass 2 writes selection bitmaps where its layout allows.
   const bool use_union = union_enabled() && union_supported(dtype, H, H_kv);
@@ -324,7 +326,8 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
                           use_union ? bits : nullptr, w.bits_stride, &bits_written)))
     return st;
   if ((st = mark(2))) return st;
-  if (union_enabled() && union_supported(dtype, H, H_kv)) {
+  if (passes < 3) return DCR_OK;
+  if (use_union) {
     if ((st = launch_attend_union(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
                                   idx, bits_written ? bits : nullptr, w.bits_stride, B, H, H_kv,
                                   N, k_eff, O, partials, w.part_splits, counters, s)))
@@ -355,6 +358,17 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype, int
     if (events[i] == nullptr) return DCR_ERR_NULL;
   return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
                      N, D, k_eff, eps, O, workspace, workspace_bytes, stream, events);
+}
+
+int dcr_decode_prefix(const void* Q, const void* K, const void* V, int dtype,
+                      int64_t k_stride_b, int64_t k_stride_h, int64_t v_stride_b,
+                      int64_t v_stride_h, int B, int H, int H_kv, int N, int D, int k_eff,
+                      float eps, void* O, void* workspace, size_t workspace_bytes, void* stream,
+                      int passes) {
+  if (passes < 1 || passes > 3) return DCR_ERR_SHAPE;
+  return decode_impl(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h, B, H, H_kv,
+                     N, D, k_eff, eps, O, workspace, workspace_bytes, stream, nullptr, nullptr,
+                     passes);
 }
 
 // ---- projected-score mode --------------------------------------------------------------

@@ -55,6 +55,8 @@ SIGNATURES = {
     "dcr_decode_timed": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
                                 _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp,
                                 ctypes.POINTER(_vp)]),
+    "dcr_decode_prefix": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _i32, _i32, _i32,
+                                 _i32, _i32, _i32, _f32, _vp, _vp, _sz, _vp, _i32]),
     "dcr_project_keys": (_i32, [_vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp,
                                 _i64, _i64, _vp]),
     "dcr_cache_append": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _vp,

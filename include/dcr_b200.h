@@ -163,6 +163,17 @@ int dcr_decode_timed(const void* Q, const void* K, const void* V, int dtype,
                      void* O, void* workspace, size_t workspace_bytes, void* stream,
                      void* const* events);
 
+/* The first `passes` (1, 2 or 3) passes of dcr_decode, launched exactly as dcr_decode
+ * launches them (Pass 2 writes the selection in the form the decode step's Pass 3 reads),
+ * for timing each pass as its marginal cost inside the step. Diagnostic: the reference has
+ * no counterpart. */
+int dcr_decode_prefix(const void* Q, const void* K, const void* V, int dtype,
+                      int64_t k_stride_b, int64_t k_stride_h,
+                      int64_t v_stride_b, int64_t v_stride_h,
+                      int B, int H, int H_kv, int N, int D, int k_eff, float eps,
+                      void* O, void* workspace, size_t workspace_bytes, void* stream,
+                      int passes);
+
 /* ---------------------------------------------------------------------------------
  * Projected-score mode. No counterpart in the reference (its Pass 1 always reads the
  * 64-dim keys): the cache also holds KP = K . P, the keys projected by a fixed
