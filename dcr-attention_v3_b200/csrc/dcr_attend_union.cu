@@ -147,6 +147,24 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   const int wstride = p.span >> 5;  // words per head in hbits
   const int64_t row0 = static_cast<int64_t>(b) * p.H + static_cast<int64_t>(hk) * G;  // head 0
 
+  // ---- Q as the A operand: row r = lane / 4 is head r (rows >= G and 8..15 are zero);
+  // loaded first, so that its latency overlaps the list building below ----
+  const int hr = lane >> 2;  // head row of this lane's accumulators (c0, c1)
+  const int q4 = lane & 3;
+  const bool head_ok = hr < G;
+  uint32_t aq[4][4];
+  {
+    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+        static_cast<const uint8_t*>(p.q) + (row0 + (head_ok ? hr : 0)) * 128);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      aq[kk][0] = head_ok ? __ldg(qrow + 8 * kk + q4) : 0u;      // dims 16kk + 2q4, +1
+      aq[kk][1] = 0u;
+      aq[kk][2] = head_ok ? __ldg(qrow + 8 * kk + 4 + q4) : 0u;  // dims 16kk + 8 + 2q4, +1
+      aq[kk][3] = 0u;
+    }
+  }
+
   // ---- the union of the G heads' selections inside [lo, hi): word tid of each head -------
   uint32_t hw[kUnMaxG];
 #pragma unroll
@@ -271,23 +289,6 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   };
 #pragma unroll
   for (int i = 0; i < kUnStages - 1; ++i) issue(i);
-
-  // ---- Q as the A operand: row r = lane / 4 is head r (rows >= G and 8..15 are zero) ----
-  const int hr = lane >> 2;  // head row of this lane's accumulators (c0, c1)
-  const int q4 = lane & 3;
-  const bool head_ok = hr < G;
-  uint32_t aq[4][4];
-  {
-    const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-        static_cast<const uint8_t*>(p.q) + (row0 + (head_ok ? hr : 0)) * 128);
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      aq[kk][0] = head_ok ? __ldg(qrow + 8 * kk + q4) : 0u;      // dims 16kk + 2q4, +1
-      aq[kk][1] = 0u;
-      aq[kk][2] = head_ok ? __ldg(qrow + 8 * kk + 4 + q4) : 0u;  // dims 16kk + 8 + 2q4, +1
-      aq[kk][3] = 0u;
-    }
-  }
 
   float m_run = -INFINITY;  // this head row's running maximum (log2 units)
   float l_part = 0.0f;      // this lane's share of the row's sum
