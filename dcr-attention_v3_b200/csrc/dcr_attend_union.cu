@@ -5,10 +5,12 @@
 // separately; the G query heads of one KV head select overlapping rows (at c = 0.15 and
 // G = 4 the union is ~78% of the per-head total), so L2 and the SMs move every shared row up
 // to G times. Here a CTA takes one (b, h_kv) group and one range of positions, builds the
-// union of the G heads' selections inside the range from their ascending index lists, and
-// gathers each union row once. All G heads are scored against every union row and the rows
-// a head did not select are masked: masked dense work, which on CUDA cores cost 3x the
-// arithmetic of the selected pairs, is cheap on the tensor cores.
+// union of the G heads' selections inside the range — from the selection bitmaps Pass 2
+// writes in the decode step (G words per thread), or, where Pass 2 wrote index lists, by
+// searching each head's ascending list — and gathers each union row once. All G heads are
+// scored against every union row and the rows a head did not select are masked: masked
+// dense work, which on CUDA cores cost 3x the arithmetic of the selected pairs, is cheap
+// on the tensor cores.
 //
 // Per 64-row tile, warp w takes union rows [16w, 16w + 16):
 //   S = Q K^T   mma.sync m16n8k16 (rows: the G heads, zero-padded to 16; fp32 accumulation
