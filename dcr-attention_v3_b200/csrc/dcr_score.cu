@@ -163,7 +163,17 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-template <typename T, int G>
+// Order key of a bf16 score without branches, equal to bf16_order_key for all 65536
+// patterns: -0 sorts as +0, every NaN on top.
+__device__ __forceinline__ uint32_t bf16_order_key_lean(uint32_t b) {
+  const uint32_t m = b & 0x7fffu;
+  const uint32_t neg = (b >> 15) & (m != 0u ? 1u : 0u);
+  const uint32_t key = neg ? (m ^ 0x7fffu) : (m | 0x8000u);
+  return m > 0x7f80u ? 0xffffu : key;
+}
+
+// kKeys: store order keys (the decode steps) instead of bf16 bits (p.keys_out).
+template <typename T, int G, bool kKeys>
 __global__ void __launch_bounds__(kP1Threads, (p1_ctas_per_sm<T, G>()))
     score_kernel(const __grid_constant__ CUtensorMap kmap, const P1Params p) {
   using Cfg = P1Cfg<T>;
@@ -353,7 +363,7 @@ __global__ void __launch_bounds__(kP1Threads, (p1_ctas_per_sm<T, G>()))
 #pragma unroll
       for (int j = 0; j < G; ++j) {
         uint32_t bits = f32_to_bf16_bits(res[i][j]);
-        if (p.keys_out) bits = bf16_order_key(bits);
+        if constexpr (kKeys) bits = bf16_order_key_lean(bits);
         sc[j * kTR + tid + i * kP1Threads] = static_cast<uint16_t>(bits);
       }
 
@@ -413,11 +423,15 @@ static int launch_score_t(const void* K, int64_t ksb, int64_t ksh, const P1Param
   if (r != CUDA_SUCCESS) return DCR_ERR_CUDA;
 
   constexpr int smem = p1_smem_bytes<T, G>();
-  if (ensure_smem_attr(reinterpret_cast<const void*>(&score_kernel<T, G>), smem) != cudaSuccess)
-    return DCR_ERR_CUDA;
+  const void* fn = p.keys_out ? reinterpret_cast<const void*>(&score_kernel<T, G, true>)
+                              : reinterpret_cast<const void*>(&score_kernel<T, G, false>);
+  if (ensure_smem_attr(fn, smem) != cudaSuccess) return DCR_ERR_CUDA;
   const int max_ctas = device_sm_count() * p1_ctas_per_sm<T, G>();
   const int grid = p.total_tiles < max_ctas ? p.total_tiles : max_ctas;
-  score_kernel<T, G><<<grid, kP1Threads, smem, st>>>(map, p);
+  if (p.keys_out)
+    score_kernel<T, G, true><<<grid, kP1Threads, smem, st>>>(map, p);
+  else
+    score_kernel<T, G, false><<<grid, kP1Threads, smem, st>>>(map, p);
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }
 
