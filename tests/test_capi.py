@@ -113,3 +113,10 @@ def test_argument_errors_return_before_any_launch(lib):
     assert lib.dcr_select(16, 100, 4, 100, 100, 16, None) == 3
     assert lib.dcr_select(16, 50, 4, 100, 10, 16, None) == 2         # stride < N
     assert lib.dcr_unit_query(16, 0, 1, 1, 32, ctypes.c_float(1e-12), 16, None) == 2
+    # the step-prefix diagnostic takes 1, 2 or 3 passes and validates like dcr_decode
+    for passes in (0, 4):
+        assert lib.dcr_decode_prefix(16, 16, 16, 0, 8 * 128 * 64, 128 * 64, 8 * 128 * 64,
+                                     128 * 64, 1, 32, 8, 128, 64, 10, 1e-12, 16, 16, 1 << 20,
+                                     None, passes) == 2
+    assert lib.dcr_decode_prefix(16, 16, 16, 0, 8 * 128 * 64, 128 * 64, 8 * 128 * 64, 128 * 64,
+                                 1, 32, 8, 128, 32, 10, 1e-12, 16, 16, 1 << 20, None, 1) == 2
