@@ -608,6 +608,16 @@ int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, in
   return DCR_OK;
 }
 
+int dcr_binary_version(int* version_out) {
+  if (version_out == nullptr) return DCR_ERR_NULL;
+  cudaFuncAttributes a{};
+  if (cudaFuncGetAttributes(&a, reinterpret_cast<const void*>(&dcr::unit_query_kernel<__half>)) !=
+      cudaSuccess)
+    return DCR_ERR_CUDA;
+  *version_out = a.binaryVersion;
+  return DCR_OK;
+}
+
 int dcr_read_device_status(int* status_out, int clear) {
   if (status_out == nullptr) return DCR_ERR_NULL;
   if (cudaDeviceSynchronize() != cudaSuccess) return DCR_ERR_CUDA;

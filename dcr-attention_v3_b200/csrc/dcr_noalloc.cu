@@ -3,10 +3,10 @@
 // Why it exists: dcr_decode needs a workspace (scores, selected indices, split-K
 // partials, tickets) that the caller allocates. Some callers cannot allocate device memory
 // at the point where they run a decode step: an inference-engine plugin whose enqueue
-// function must not allocate (the engine owns all device memory), code running inside a
-// host callback, or a latency-critical serving loop that cannot afford cudaMalloc's
-// implicit device synchronisation. For them this entry point runs the same three kernels
-// on scratch memory that lives in a file-scope __device__ array of this library.
+// function must not allocate (the engine owns all device memory), or a latency-critical
+// serving loop that cannot afford cudaMalloc's implicit device synchronisation. For them
+// this entry point runs the same three kernels on scratch memory that lives in a
+// file-scope __device__ array of this library.
 //
 // Limits and sharing rules:
 //  - The array holds DCR_NOALLOC_SCRATCH_BYTES (16 MiB). Every GPU on which the library's
@@ -21,8 +21,10 @@
 //    every call before Pass 3 uses it; scores, indices and partials are fully written
 //    before they are read.
 //  - The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current). Make that first call before any
-//    stream capture begins.
+//    (cudaGetSymbolAddress, with that device current; the driver may load the library's
+//    module then) and sets the kernels' shared-memory attributes. Make that first call a
+//    warm-up during the caller's initialisation, outside its no-allocation region and
+//    before any stream capture begins; later calls allocate nothing.
 //  - The entry point calls no cudaMalloc, cudaFree or other device allocator.
 #include <cuda_runtime.h>
 

@@ -107,6 +107,7 @@ SIGNATURES = {
                                            ctypes.POINTER(_vp), _i32, _i32, _i32, _vp, _vp, _sz,
                                            _vp, ctypes.POINTER(_vp)]),
     "dcr_read_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
+    "dcr_binary_version": (_i32, [ctypes.POINTER(_i32)]),
 }
 
 _lib = None

@@ -138,15 +138,18 @@ int dcr_decode(const void* Q, const void* K, const void* V, int dtype,
                void* O, void* workspace, size_t workspace_bytes, void* stream);
 
 /* dcr_decode without a caller workspace, for callers that cannot allocate device memory
- * where they run a decode step (an engine plugin whose enqueue must not allocate, a host
- * callback, a serving loop that cannot take cudaMalloc's implicit synchronisation).
+ * where they run a decode step (an engine plugin whose enqueue must not allocate because
+ * the engine owns all device memory, a serving loop that cannot take cudaMalloc's
+ * implicit synchronisation).
  * No counterpart in the reference: its Python path allocates through torch on every call.
  * Scratch is a 16 MiB (DCR_NOALLOC_SCRATCH_BYTES) __device__ array inside the library,
  * held by every GPU that loads the library until exit; shapes whose dcr_workspace_bytes
  * exceed it return DCR_ERR_NOALLOC_LIMIT and launch nothing. All calls on a device share
  * the array: calls that overlap on the GPU race, calls ordered on one stream do not.
- * The first call on a device looks up the array's address; make it before any stream
- * capture begins. Allocates nothing. */
+ * The first call on a device looks up the array's address and sets kernel attributes
+ * (the driver may load the module then): make it a warm-up at initialisation, outside
+ * the no-allocation region and before any stream capture begins. Later calls allocate
+ * nothing. */
 int dcr_decode_noalloc(const void* Q, const void* K, const void* V, int dtype,
                        int64_t k_stride_b, int64_t k_stride_h,
                        int64_t v_stride_b, int64_t v_stride_h,
@@ -358,6 +361,11 @@ int dcr_shard_decode_peer_timed(const void* Q, const void* K, const void* V, int
  * status bits (DCR_ERR_DEVICE_*) set since the last clear; clears them if clear != 0.
  * Diagnostic: the reference has no counterpart (its kernels have no device status). */
 int dcr_read_device_status(int* status_out, int clear);
+
+/* Writes the compute capability the library's device code was built for, as the CUDA
+ * runtime reports it for the current device (cudaFuncGetAttributes().binaryVersion:
+ * 100 for sm_100a). Diagnostic: the reference has no counterpart. */
+int dcr_binary_version(int* version_out);
 
 /* ---- native step runner (dcr_runner.cu) ------------------------------------------
  * One decode step over fixed caches — the H2D copy of the step's query from pinned

@@ -40,7 +40,15 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, _HERE)
 from cases import CASES, build_inputs, fixture_path, input_sha256  # noqa: E402
 
-REF = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REF = os.environ.get("REFERENCE_ROOT")
+
+
+def _reference_root() -> str:
+    """The reference checkout to import: REFERENCE_ROOT is required (no default path)."""
+    if not REF or not os.path.isdir(os.path.join(REF, "dcr_attention")):
+        raise SystemExit("set REFERENCE_ROOT to a checkout of Seqev/dcr-attention_v3 "
+                         "(the directory that holds the dcr_attention package)")
+    return REF
 
 
 def _bits(t: torch.Tensor) -> np.ndarray:
@@ -48,7 +56,7 @@ def _bits(t: torch.Tensor) -> np.ndarray:
 
 
 def main() -> None:
-    sys.path.insert(0, REF)
+    sys.path.insert(0, _reference_root())
     from dcr_attention.kernel import qaxis_topk_reference as R  # noqa: E402
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))

@@ -41,6 +41,15 @@ def _bf16_tensor(bits: np.ndarray, shape) -> torch.Tensor:
     return torch.from_numpy(bits.astype(np.uint16).view(np.int16)).view(torch.bfloat16).reshape(shape)
 
 
+def test_binary_version(cuda_lib):
+    """The runtime reports the library's device code as built for compute capability 10.0
+    (sm_100a), the only architecture the build compiles."""
+    import ctypes
+    v = ctypes.c_int(0)
+    assert cuda_lib.dcr_binary_version(ctypes.byref(v)) == 0
+    assert v.value == 100
+
+
 # ---------------------------------------------------------------------------------------
 # Golden vectors (made by the reference itself)
 # ---------------------------------------------------------------------------------------
