@@ -72,6 +72,44 @@ class TorchComm:
         return out
 
 
+class ShardMismatchError(ValueError):
+    """The ranks of a sharded step disagree on what the step is (raised on every rank)."""
+
+
+_DTYPE_IDS = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def agree_on_step(comm, *, B: int, H: int, H_kv: int, N_local: int, k_eff: int,
+                  dtype: torch.dtype, device=None):
+    """Checks, with one all-gather, that every rank describes the same step, and returns
+    (the ranks' chunk lengths, this rank's offset, the whole context's length).
+
+    Every rank must pass the same B, H, H_kv, k_eff and dtype (N_local may differ: it is
+    each rank's chunk). The exact global top-K depends on all of them: a rank with another
+    k_eff would select from other histogram bins than its peers and the combined set would
+    not be the reference's. Every rank sees the same gathered values, so every rank raises
+    the same :class:`ShardMismatchError` (or none); no rank is left waiting in a later
+    collective. Then ``0 < k_eff < sum(N_r)`` is checked as in the single-GPU step."""
+    meta = torch.tensor([B, H, H_kv, int(N_local), int(k_eff), _DTYPE_IDS.get(dtype, -1)],
+                        dtype=torch.int64, device=device if device is not None else "cpu")
+    allm = comm.all_gather(meta).view(comm.world, -1).cpu()
+    names = ("B", "H", "H_kv", "N_local", "k_eff", "dtype")
+    for j, name in enumerate(names):
+        if name == "N_local":
+            continue
+        vals = allm[:, j].tolist()
+        if any(v != vals[0] for v in vals):
+            raise ShardMismatchError(
+                f"ranks disagree on {name}: {vals} (rank-ordered); every rank of a sharded "
+                f"step must pass the same B, H, H_kv, k_eff and dtype")
+    n_locals = [int(x) for x in allm[:, 3].tolist()]
+    if any(n <= 0 for n in n_locals):
+        raise ShardMismatchError(f"every rank needs a non-empty chunk, got N_local={n_locals}")
+    n_total = sum(n_locals)
+    check_k_range(int(k_eff), n_total)
+    return n_locals, sum(n_locals[: comm.rank]), n_total
+
+
 def sequence_shard_step(step, comm, bufs: Optional[dict] = None):
     """One decode step of the sequence split: the per-rank phases of ``step`` with the
     three collectives between them. Returns O [B, H, D] (identical on every rank).
@@ -242,7 +280,8 @@ class SequenceShardedDecoder:
     """Decode steps of one layer whose KV cache is split by sequence across the ranks.
 
     Construct once per (shape, group): it learns every rank's chunk length with one
-    all-gather, checks ``0 < k_eff < sum(N_r)`` (the reference's caller-side contract,
+    all-gather that also checks that the ranks agree on the step (:func:`agree_on_step`),
+    checks ``0 < k_eff < sum(N_r)`` (the reference's caller-side contract,
     dcr_attention/models/llama/attention.py:806) and allocates the step's buffers. Each
     call runs :func:`sequence_shard_step` and returns O [B, H, D] on every rank."""
 
@@ -253,11 +292,9 @@ class SequenceShardedDecoder:
         self.device = torch.device(device)
         self.comm = comm if comm is not None else TorchComm(group)
         self.exchange = exchange
-        n = torch.tensor([N_local], dtype=torch.int64, device=self.device)
-        self.n_locals = [int(x) for x in self.comm.all_gather(n).view(-1).tolist()]
-        self.offset = sum(self.n_locals[: self.comm.rank])
-        self.n_total = sum(self.n_locals)
-        check_k_range(int(k_eff), self.n_total)
+        self.n_locals, self.offset, self.n_total = agree_on_step(
+            self.comm, B=B, H=H, H_kv=H_kv, N_local=N_local, k_eff=k_eff, dtype=dtype,
+            device=self.device)
         self.step = CudaSequenceShardStep(B, H, H_kv, N_local, k_eff, dtype=dtype,
                                           device=self.device, eps=eps)
         rows, W = B * H, self.comm.world

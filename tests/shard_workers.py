@@ -171,3 +171,106 @@ def tp_model_rank(rank: int, world: int, port: int, out_dir: str) -> None:
     dist.barrier()
     torch.save(res, os.path.join(out_dir, f"tp{rank}.pt"))
     dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------
+# Host-side failure injection (gloo ranks on CPU; no GPU is involved)
+# ---------------------------------------------------------------------------------------
+class FaultyComm:
+    """A TorchComm whose rank `victim` raises at its `fail_at`-th collective (0-based), the
+    way a rank whose host code fails mid-step would leave its peers."""
+
+    def __init__(self, comm, victim: int, fail_at: int):
+        self.comm, self.victim, self.fail_at, self.calls = comm, victim, fail_at, 0
+        self.world, self.rank = comm.world, comm.rank
+
+    def _tick(self):
+        n = self.calls
+        self.calls += 1
+        if self.rank == self.victim and n == self.fail_at:
+            raise RuntimeError("injected fault on rank %d at collective %d" % (self.rank, n))
+
+    def all_reduce_sum_(self, t):
+        self._tick()
+        return self.comm.all_reduce_sum_(t)
+
+    def all_gather(self, t, out=None):
+        self._tick()
+        return self.comm.all_gather(t, out)
+
+    def barrier(self):
+        self._tick()
+        self.comm.barrier()
+
+
+def gloo_fault_rank(rank: int, world: int, port: int, out_dir: str, scenario: str,
+                    timeout_s: float) -> None:
+    """One rank of a sequence-split decode with a host-side fault in `scenario`:
+
+    * ``raise_mid_step``: the last rank raises at its second collective of step 0;
+    * ``leave_between_steps``: the last rank exits after step 0 without tearing down;
+    * ``stall``: the last rank sleeps for 3 process-group timeouts before step 1;
+    * ``disagree_k``: the last rank passes k_eff + 2;
+    * ``disagree_heads``: the last rank passes other head counts.
+
+    Writes ``rank{r}.json`` with what this rank saw, then leaves with os._exit."""
+    _paths()
+    import json
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from dcr_b200.sharded import ShardMismatchError, TorchComm, agree_on_step, sequence_shard_step
+    from dcr_b200.synthetic import make_decode_inputs
+    from oracle.shard_protocol import OracleSequenceShardStep
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    victim = world - 1
+    rec = {"rank": rank, "steps_ok": 0}
+
+    def done(outcome, err=None, t0=None):
+        rec["outcome"] = outcome
+        if err is not None:
+            rec["type"] = type(err).__name__
+            rec["msg"] = str(err)[:300]
+        if t0 is not None:
+            rec["elapsed_s"] = time.perf_counter() - t0
+        with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+            json.dump(rec, f)
+        os._exit(0)
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+    B, H, H_kv, n_local = 1, 8, 2, 300
+    N = n_local * world
+    k = 90
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=5)
+    Kc = K[:, :, rank * n_local:(rank + 1) * n_local].contiguous()
+    Vc = V[:, :, rank * n_local:(rank + 1) * n_local].contiguous()
+    base = TorchComm()
+    comm = FaultyComm(base, victim, 1) if scenario == "raise_mid_step" else base
+    my_k = k + 2 if (scenario == "disagree_k" and rank == victim) else k
+    my_H, my_Hkv = (16, 4) if (scenario == "disagree_heads" and rank == victim) else (H, H_kv)
+    t0 = time.perf_counter()
+    try:
+        agree_on_step(base, B=B, H=my_H, H_kv=my_Hkv, N_local=n_local, k_eff=my_k,
+                      dtype=torch.bfloat16)
+    except ShardMismatchError as e:
+        done("mismatch", e, t0)
+    for step_i in range(2):
+        if scenario == "leave_between_steps" and rank == victim and step_i == 1:
+            done("left")
+        if scenario == "stall" and rank == victim and step_i == 1:
+            time.sleep(3 * timeout_s)
+        t0 = time.perf_counter()
+        try:
+            step = OracleSequenceShardStep(Q, Kc, Vc, k)
+            O = sequence_shard_step(step, comm)
+            if not torch.isfinite(O).all():
+                done("bad_output")
+            rec["steps_ok"] += 1
+        except RuntimeError as e:
+            done("injected" if "injected fault" in str(e) else "error", e, t0)
+    done("ok")
