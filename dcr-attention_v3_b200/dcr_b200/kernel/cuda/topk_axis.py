@@ -40,6 +40,21 @@ def _check_qk(Q: torch.Tensor, K_cache: torch.Tensor):
     return B, H, H_kv, N, dt
 
 
+def check_attention_args(Q: torch.Tensor, K_cache: torch.Tensor, V_cache: torch.Tensor,
+                         k_eff: int):
+    """The argument checks of :func:`topk_qaxis_attention` (the reference's
+    topk_axis.py:37-44 and fused_attn.py:170-193, widened as the module docstring says).
+    Returns (B, H, H_kv, N, dtype code, K's batch and head strides, V's)."""
+    B, H, H_kv, N, dt = _check_qk(Q, K_cache)
+    _lib.require_cuda(V_cache)
+    require(tuple(V_cache.shape) == tuple(K_cache.shape), "V_cache must match K_cache's shape")
+    require(V_cache.dtype == Q.dtype, f"V_cache must have Q's dtype {Q.dtype}")
+    check_k_range(int(k_eff), N)
+    ksb, ksh = cache_strides(K_cache, "K_cache")
+    vsb, vsh = cache_strides(V_cache, "V_cache")
+    return B, H, H_kv, N, dt, ksb, ksh, vsb, vsh
+
+
 def compute_u_Q(Q: torch.Tensor, eps: float = 1e-12) -> torch.Tensor:
     """u = f32(Q) / max(||f32(Q)||, eps) on the device (``_compute_u_Q``,
     qaxis_topk_reference.py:42)."""
@@ -90,13 +105,7 @@ def topk_qaxis_attention(
     workspace_buf: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:              # [B, H, D], Q's dtype
     """Full decode step: unit query, Pass 1 scores, Pass 2 top-K, Pass 3 attention."""
-    B, H, H_kv, N, dt = _check_qk(Q, K_cache)
-    _lib.require_cuda(V_cache)
-    require(tuple(V_cache.shape) == tuple(K_cache.shape), "V_cache must match K_cache's shape")
-    require(V_cache.dtype == Q.dtype, f"V_cache must have Q's dtype {Q.dtype}")
-    check_k_range(int(k_eff), N)
-    ksb, ksh = cache_strides(K_cache, "K_cache")
-    vsb, vsh = cache_strides(V_cache, "V_cache")
+    B, H, H_kv, N, dt, ksb, ksh, vsb, vsh = check_attention_args(Q, K_cache, V_cache, k_eff)
     if out is None:
         out = torch.empty(B, H, HEAD_DIM, dtype=Q.dtype, device=Q.device)
     else:
