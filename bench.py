@@ -113,9 +113,9 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 # CPU baseline: the C oracle (restatement of the reference's algorithm), all host threads
 # ---------------------------------------------------------------------------------------
-def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s, max_groups=None):
-    """Seconds per full layer-step of the C oracle, timed on a bounded sample of the
-    layer's batch rows and scaled by rows (the work is linear in B)."""
+def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s):
+    """Seconds per full layer-step (all B batch rows) of the C oracle with all host threads:
+    median over as many runs as fit in budget_s (at least 3)."""
     import numpy as np
     import torch
     from dcr_b200.synthetic import make_decode_inputs
@@ -123,8 +123,7 @@ def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s, max_groups=
 
     oracle.build()
     torch_dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dtype_name]
-    b_sample = 1  # one batch row (8 KV heads, 32 query heads) per sample
-    Q, K, V = make_decode_inputs(b_sample, H, H_kv, N, dtype=torch_dt, seed=seed)
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch_dt, seed=seed)
 
     def bits(t):
         t = t.contiguous()
@@ -134,13 +133,51 @@ def cpu_reference_time(B, H, H_kv, N, k, dtype_name, seed, budget_s, max_groups=
     oracle.decode(q, kk, vv, dtype_name, k)  # warm-up
     times = []
     t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 2:
+    while time.perf_counter() < t_end or len(times) < 3:
         t0 = time.perf_counter()
         oracle.decode(q, kk, vv, dtype_name, k)
         times.append(time.perf_counter() - t0)
-    per_layer = statistics.median(times) * (B / b_sample)
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    return per_layer, threads, len(times), b_sample
+    return statistics.median(times), _omp_threads(), len(times)
+
+
+def _host_cpu():
+    """(physical cores, logical CPUs, CPU model) of this host."""
+    try:
+        import psutil
+        phys = psutil.cpu_count(logical=False) or os.cpu_count() or 1
+    except ImportError:
+        phys = os.cpu_count() or 1
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return int(phys), int(os.cpu_count() or 1), model
+
+
+def _omp_threads():
+    return int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+
+
+def bench_config(world, split, dtype):
+    """The workload description, identical in the GPU arm and the reference arm."""
+    B, H, H_kv, D = CFG["B"], CFG["H"], CFG["H_kv"], CFG["D"]
+    seq = split == "seq"
+    N = CFG["N"] * (world if seq else 1)
+    cfg = {"workload": _workload_name(world, split), "B": B, "N": N, "H": H, "H_kv": H_kv,
+           "D": D, "k_eff": _k_eff(N, CFG["coverage"]), "coverage": CFG["coverage"],
+           "dtype": dtype,
+           "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
+                 f"{2 * B * H_kv * CFG['N'] * D * 2 / 1e6:.0f} MB per GPU"}
+    if world > 1:
+        cfg["parallelism"] = (f"sequence split over {world} GPUs, exact global top-K" if seq
+                              else f"KV-head split over {world} GPUs")
+    else:
+        cfg["parallelism"] = "one GPU"
+    return cfg
 
 
 def _workload_name(world, split):
@@ -153,44 +190,60 @@ def _workload_name(world, split):
 
 
 def run_reference_arm(args):
+    """The reference's algorithm on the host CPU: the C oracle (a restatement of
+    topk_qaxis_attention_reference) with all host threads, each step one full layer-step of
+    the GPU arm's workload (every batch row), same config, metric and unit."""
     rank, world, _ = _env()
     if rank != 0:
         return 0
     B, H, H_kv = CFG["B"], CFG["H"], CFG["H_kv"]
-    N = CFG["N"] * (world if args.split == "seq" else 1)  # the whole job's context
-    k = _k_eff(N, CFG["coverage"])
-    # each step = one sample (batch row 0) of the layer; value scaled to the full layer
+    cfg = bench_config(world, args.split, args.dtype)
+    N, k = cfg["N"], cfg["k_eff"]
+    import numpy as np
     import torch
     from dcr_b200.synthetic import make_decode_inputs
     from oracle import oracle
     oracle.build()
-    threads = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-    Q, K, V = make_decode_inputs(1, H, H_kv, N, dtype=torch.float16, seed=0)
-    bits = lambda t: t.contiguous().view(torch.int16).numpy().view("uint16")  # noqa: E731
+    threads = _omp_threads()
+    phys, logical, model = _host_cpu()
+    torch_dt = {"f16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch_dt, seed=0)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
     q, kk, vv = bits(Q), bits(K), bits(V)
+    # a full layer-step per step; past ~150 s for the whole run (long contexts at many GPUs)
+    # each step is a sample of the batch rows, scaled by B / rows
+    t0 = time.perf_counter()
+    oracle.decode(q, kk, vv, args.dtype, k)
+    t_one = time.perf_counter() - t0
+    rows = B
+    while rows > 1 and t_one * rows / B * (args.steps + args.warmup) > 150.0:
+        rows //= 2
+    if rows < B:
+        q, kk, vv = q[:rows], kk[:rows], vv[:rows]
     for _ in range(args.warmup):
-        oracle.decode(q, kk, vv, "f16", k)
+        oracle.decode(q, kk, vv, args.dtype, k)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.decode(q, kk, vv, "f16", k)
-    dt = (time.perf_counter() - t0) / args.steps * B  # scale one batch row to B rows
-    value = dt * 1e6
+        oracle.decode(q, kk, vv, args.dtype, k)
+    value = (time.perf_counter() - t0) / args.steps * (B / rows) * 1e6
+    sample = ("full layer: every step is the whole B=%d layer-step (32 q-heads, N=%d)" % (B, N)
+              if rows == B else
+              "batch rows 0..%d of the B=%d layer-step (N=%d) per step, scaled x%g"
+              % (rows - 1, B, N, B / rows))
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 2), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(value / 1e3, 4), "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "weak" if args.split == "seq" else "strong",
         "vs_baseline": round(value / PUBLISHED_US_PER_LAYER, 5) if world == 1 else None,
         "vs_baseline_note": PUBLISHED_NOTE if world == 1 else None,
-        "dtype": "f16", "data": "synthetic",
-        "config": {"workload": _workload_name(world, args.split), "B": B, "N": N, "H": H,
-                   "H_kv": H_kv, "D": 64, "k_eff": k, "coverage": CFG["coverage"],
-                   "parallelism": "cpu"},
+        "dtype": args.dtype, "data": "synthetic",
+        "config": cfg,
         "cpu_baseline": {"value": round(value, 2), "unit": UNIT, "cores": threads,
+                         "physical_cores": phys, "logical_cpus": logical, "cpu_model": model,
                          "kind": "port",
                          "sample": "C oracle (oracle/dcr_oracle.c, OpenMP) restating "
-                                   "topk_qaxis_attention_reference; each step = batch row 0 "
-                                   f"(32 q-heads, N={N}) scaled x{B} to the B={B} layer"},
+                                   "topk_qaxis_attention_reference; " + sample},
         "e2e": {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -452,8 +505,10 @@ def run_gpu_arm(args):
     union_rows /= min(steps, 8)
 
     bytes_p1 = B * H_kv * N * D * eb + B * H * N * 2 + B * H * D * eb
-    bytes_p2 = B * H * N * 2 + B * H * k * 4
-    bytes_p3 = union_rows * 2 * D * eb + B * H * k * 4 + 2 * B * H * D * eb
+    # the decode step's Pass 2 reads the keys and writes selection bitmaps (N/8 bytes per
+    # row); Pass 3 reads the bitmaps, the union rows' K and V, Q, and writes O
+    bytes_p2 = B * H * N * 2 + B * H * N // 8
+    bytes_p3 = union_rows * 2 * D * eb + B * H * N // 8 + 2 * B * H * D * eb
     peak, peak_kind = _peaks()
     kern = {
         "pass1_score": {"us": round(p1, 2), "bytes": bytes_p1, "gbs": round(bytes_p1 / p1 / 1e3, 1)},
@@ -564,6 +619,14 @@ def run_gpu_arm(args):
     model_e2e = None
     if world == 1 and not args.no_model:
         model_e2e = model_decode_bench(dev, args.model_steps, stream)
+    del caches, kps, sc_layers, idx_layers
+    torch.cuda.empty_cache()
+    sweep = None
+    if not args.no_sweep:
+        sweep = sweep_bench(dev, args.sweep_steps, args.dtype)
+    model_tp = None
+    if not args.no_model:
+        model_tp = _model_tp_safe(dev, 1, 0, args.model_tp_steps)
 
     # max over ranks
     t = torch.tensor([ms, e2e_ms, ms_eager, e2e_eager_ms], dtype=torch.float64, device=dev)
@@ -573,13 +636,15 @@ def run_gpu_arm(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        per_layer, threads, n, bs = cpu_reference_time(B, H, H_kv, N, k, args.dtype, 0,
-                                                       budget_s=args.cpu_budget)
-        cpu = {"value": round(per_layer * 1e6, 1), "unit": UNIT, "cores": threads, "kind": "port",
+        per_layer, threads, n = cpu_reference_time(B, H, H_kv, N, k, args.dtype, 0,
+                                                    budget_s=args.cpu_budget)
+        phys, logical, model = _host_cpu()
+        cpu = {"value": round(per_layer * 1e6, 1), "unit": UNIT, "cores": threads,
+               "physical_cores": phys, "logical_cpus": logical, "cpu_model": model,
+               "kind": "port",
                "sample": f"C oracle (oracle/dcr_oracle.c, OpenMP, restating the reference's "
-                         f"topk_qaxis_attention_reference) on batch row 0 of the layer "
-                         f"(32 q-heads, N={N}), median of {n} runs over ~{args.cpu_budget:.0f} s, "
-                         f"scaled x{B // bs} to the B={B} layer"}
+                         f"topk_qaxis_attention_reference) on the full B={B} layer-step "
+                         f"(32 q-heads, N={N}), median of {n} runs over ~{args.cpu_budget:.0f} s"}
 
     value = ms * 1e3 / (steps * world)
     line = {
@@ -588,14 +653,8 @@ def run_gpu_arm(args):
         "higher_is_better": False, "scaling": "weak",
         "vs_baseline": round(value / PUBLISHED_US_PER_LAYER, 5), "vs_baseline_note": PUBLISHED_NOTE,
         "dtype": args.dtype, "data": "synthetic",
-        "config": {"workload": "config1 hero single-layer decode (fresh Q per step)",
-                   "B_per_rank": B, "N": N, "H": H, "H_kv": H_kv, "D": D, "k_eff": k,
-                   "coverage": CFG["coverage"],
-                   "parallelism": f"{world} rank(s), each its own (b, h_kv) shard" if world > 1
-                   else "single GPU",
-                   "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
-                         f"{2 * B * H_kv * N * D * eb / 1e6:.0f} MB",
-                   "launch": "the K timed steps replayed as one CUDA graph",
+        "config": bench_config(world, "seq", args.dtype),
+        "timing": {"launch": "the K timed steps replayed as one CUDA graph",
                    "eager_us_per_step": round(ms_eager * 1e3 / steps, 3),
                    "clock_soak_s": args.soak},
         "roofline": {"kernel": dom_name, "bound": "hbm", "achieved": dom["gbs"], "peak": peak,
@@ -613,6 +672,8 @@ def run_gpu_arm(args):
                 "eager_api": "dcr_b200.kernel.cuda.topk_qaxis_attention called per step, "
                              "pinned host Q in / O out, host sync per step"},
         "model_e2e": model_e2e,
+        "model_tp": model_tp,
+        "sweep": sweep,
         "gpu_launches": 3 * steps,
         "device_status": status,
         "clocks": clocks,
@@ -905,6 +966,13 @@ def run_sharded_arm(args):
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, e2e_ms, ms_eager = float(t[0]), float(t[1]), float(t[2])
     value = ms * 1e3 / steps
+    if seq:
+        dec.close()
+    del caches
+    torch.cuda.empty_cache()
+    model_tp = None
+    if not args.no_model and H_kv % world == 0:
+        model_tp = _model_tp_safe(dev, world, rank, args.model_tp_steps)
     # our kernels per step; seq: score, 2 histograms, count, emit, attend, combine;
     # heads: the 3 passes of dcr_decode
     launches_per_step = 7 if seq else 3
@@ -913,19 +981,15 @@ def run_sharded_arm(args):
         "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 5),
         "higher_is_better": False, "scaling": "weak" if seq else "strong",
         "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
-        "config": {"workload": _workload_name(world, args.split), "B": B, "N": N,
-                   "N_per_gpu": n_local, "H": H, "H_kv": H_kv, "H_kv_per_gpu": h_kv_local,
-                   "D": D, "k_eff": k, "coverage": CFG["coverage"],
-                   "parallelism": (f"sequence split over {world} GPUs, exact global top-K; "
-                                   + ("histogram and state exchange pushed by the kernels "
-                                      "into the peers' buffers over NVLink (no collective)"
-                                      if args.exchange == "peer" else
-                                      "NCCL all-reduce + 2 all-gathers per layer-step"))
-                   if seq else f"KV-head split over {world} GPUs (NCCL all-gather of O)",
-                   "l2": f"inputs larger than L2: {LAYERS} rotating layer caches of "
-                         f"{2 * B * h_kv_local * n_local * D * eb / 1e6:.0f} MB per GPU",
-                   "launch": "the K timed steps (collectives included) replayed as one CUDA "
+        "config": bench_config(world, args.split, args.dtype),
+        "timing": {"launch": "the K timed steps (collectives included) replayed as one CUDA "
                              "graph",
+                   "N_per_gpu": n_local, "H_kv_per_gpu": h_kv_local,
+                   "exchange": ("histogram and state exchange pushed by the kernels into the "
+                                "peers' buffers over NVLink (no collective)"
+                                if args.exchange == "peer" else
+                                "NCCL all-reduce + 2 all-gathers per layer-step")
+                   if seq else "NCCL all-gather of O",
                    "eager_us_per_step": round(ms_eager * 1e3 / steps, 3),
                    "clock_soak_s": args.soak},
         "nccl_phases_us": phases,
@@ -936,41 +1000,36 @@ def run_sharded_arm(args):
                 "api": ("dcr_b200.sharded.SequenceShardedDecoder" if seq
                         else "dcr_b200.sharded.kv_head_sharded_attention") +
                        ", pinned host Q in / O out on every rank, host sync per step"},
+        "model_tp": model_tp,
         "gpu_launches": launches_per_step * steps,
         "device_status": status,
         "clocks": clocks,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if seq:
-        dec.close()
     dist.barrier()
     dist.destroy_process_group()
     return 0
 
 
-def run_model_tp_arm(args):
-    """``--model-tp``: BASELINE config 4 end to end — greedy decode of the 16-layer
-    Llama-3.2-1B-architecture model (random-init bf16) with B=8, caches prefilled with
-    N=262144 synthetic positions, c=0.05, split by KV head over the N ranks (one GPU each,
-    two NCCL all-reduces per layer; N=1: the unsplit model). Each step is one CUDA graph
-    per rank (H2D tokens, 16 layers, LM head, argmax, D2H tokens) with a host sync; the
-    timed `model_steps` steps follow one untimed pass over the same steps; value = ms per
-    step, max over ranks. Prints one JSON line with its own metric."""
-    import datetime
+MODEL_TP_METRIC = "model decode ms/step (config4: 16 layers, B=8, N=262144, c=.05)"
 
+
+def model_tp_bench(dev, world, rank, steps):
+    """BASELINE config 4 end to end: greedy decode of the 16-layer Llama-3.2-1B-architecture
+    model (random-init bf16) with B=8, caches prefilled with N=262144 synthetic positions,
+    c=0.05, split by KV head over the `world` ranks (one GPU each, two NCCL all-reduces per
+    layer; world 1: the unsplit model). Each step is one CUDA graph per rank (H2D tokens, 16
+    layers, LM head, argmax, D2H tokens) with a host sync; `steps` timed steps follow one
+    untimed pass over the same steps; ms per step, max over ranks. Sparse (exact top-K) and
+    dense SDPA in every layer, on the same caches and weights."""
     import torch
     import torch.distributed as dist
 
     from dcr_b200 import _lib
     from dcr_b200.models.llama.model import (DCRLlamaDecoder, GreedyDecodeGraphs,
                                               TPDCRLlamaDecoder)
-    rank, world, local = _env()
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    B, N0, c, steps = 8, 262144, 0.05, args.model_steps
+    B, N0, c = 8, 262144, 0.05
     kw = dict(attention="dcr", coverage_floor=c, dtype=torch.bfloat16, device=dev, seed=0)
     model = (TPDCRLlamaDecoder(world=world, rank=rank, **kw) if world > 1
              else DCRLlamaDecoder(**kw))
@@ -1000,28 +1059,195 @@ def run_model_tp_arm(args):
         runner.close()
         del runner
     status = _lib.read_device_status(clear=True)
-    if rank == 0:
-        k = _k_eff(N0 + 1, c)
-        print(json.dumps({
-            "metric": "model decode ms/step (config4: 16 layers, B=8, N=262144, c=.05)",
-            "value": out["dcr_exact"], "unit": "ms/step", "n_gpus": world, "steps": steps,
-            "higher_is_better": False, "scaling": "strong", "dtype": "bf16",
-            "data": "synthetic (random-init weights, seeded caches)",
-            "config": {"workload": "config4 model decode", "B": B, "N": N0, "coverage": c,
-                       "k_eff_first_step": k, "layers": 16,
-                       "parallelism": f"KV heads split over {world} GPU(s), NCCL all-reduce "
-                                      f"after o_proj and down_proj" if world > 1
-                                      else "single GPU"},
-            "ms_per_step": out,
-            "api": "dcr_b200.models.llama.model.GreedyDecodeGraphs over "
-                   + ("TPDCRLlamaDecoder" if world > 1 else "DCRLlamaDecoder"),
-            "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
-            "device_status": status}), flush=True)
     del caches, model
+    torch.cuda.empty_cache()
+    return {
+        "metric": MODEL_TP_METRIC, "value": out["dcr_exact"], "unit": "ms/step",
+        "n_gpus": world, "steps": steps, "higher_is_better": False, "scaling": "strong",
+        "dtype": "bf16", "data": "synthetic (random-init weights, seeded caches)",
+        "config": {"workload": "config4 model decode", "B": B, "N": N0, "coverage": c,
+                   "k_eff_first_step": _k_eff(N0 + 1, c), "layers": 16,
+                   "parallelism": f"KV heads split over {world} GPUs, NCCL all-reduce after "
+                                  f"o_proj and down_proj" if world > 1 else "one GPU"},
+        "ms_per_step": out,
+        "api": "dcr_b200.models.llama.model.GreedyDecodeGraphs over "
+               + ("TPDCRLlamaDecoder" if world > 1 else "DCRLlamaDecoder"),
+        "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+        "device_status": status}
+
+
+def _model_tp_safe(dev, world, rank, steps):
+    """model_tp_bench, or the error it raised (the headline line is printed either way)."""
+    try:
+        return model_tp_bench(dev, world, rank, steps)
+    except Exception as e:  # noqa: BLE001 - reported in the JSON line
+        import torch
+        torch.cuda.empty_cache()
+        return {"metric": MODEL_TP_METRIC, "error": f"{type(e).__name__}: {e}"[:300]}
+
+
+def run_model_tp_arm(args):
+    """``--model-tp``: only the config 4 model decode (model_tp_bench) over the ranks, as
+    its own JSON line."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    rank, world, local = _env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    line = model_tp_bench(dev, world, rank, args.model_tp_steps)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# ---------------------------------------------------------------------------------------
+# config 3 sweep
+# ---------------------------------------------------------------------------------------
+SWEEP_C = (0.05, 0.15, 0.30)
+SWEEP_N = (8192, 32768, 131072)
+SWEEP_B = (1, 4, 16)
+
+
+def sweep_bench(dev, n_steps, dtype_name="f16"):
+    """the single-layer step over c x N x B (GQA 32/8, head_dim 64, fp16,
+    rank-16 projection), each point timed as `n_steps` calls replayed as one CUDA graph over
+    rotating layer caches whose total exceeds L2 (CUDA events around the replay): the exact
+    step, its first one and two passes (per-pass marginal times), the projected step, and
+    torch's dense SDPA decode (enable_gqa) on the same caches."""
+    import torch
+    import torch.nn.functional as F
+
+    from dcr_b200 import _lib
+    from dcr_b200.kernel.cuda import project_keys
+    from dcr_b200.kernel.cuda._common import workspace_bytes
+    from dcr_b200.synthetic import fresh_queries, make_decode_inputs, projection_matrix
+
+    lib = _lib.load()
+    H, H_kv, D = CFG["H"], CFG["H_kv"], CFG["D"]
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16}[dtype_name]
+    dcode = _lib.DTYPE_CODES[dt]
+    peak, _ = _peaks()
+    Pd = projection_matrix(seed=0, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def graph_us(fn):
+        for i in range(2):
+            fn(i, stream.cuda_stream)
+        torch.cuda.synchronize(dev)
+        cap = torch.cuda.Stream(dev)
+        cap.wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cap):
+            for i in range(n_steps):
+                fn(i, cap.cuda_stream)
+        a = torch.cuda.Event(enable_timing=True)
+        z = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cap):
+            g.replay()
+            torch.cuda.synchronize(dev)
+            a.record(cap)
+            g.replay()
+            z.record(cap)
+        torch.cuda.synchronize(dev)
+        del g
+        return a.elapsed_time(z) * 1e3 / n_steps
+
+    points = []
+    for N in SWEEP_N:
+        for B in SWEEP_B:
+            layer_bytes = 2 * B * H_kv * N * D * 2
+            n_layers = max(2, min(32, -(-(3 * 126 * 2 ** 20) // layer_bytes)))
+            caches = [make_decode_inputs(B, H, H_kv, N, dtype=dt, device=dev,
+                                         generator=torch.Generator(device=dev).manual_seed(50 + L))[1:]
+                      for L in range(n_layers)]
+            kps = [project_keys(K, Pd) for K, _ in caches]
+            Qs = fresh_queries(n_steps, B, H, dtype=dt, seed=9, device=dev)
+            O = torch.empty(B, H, D, dtype=dt, device=dev)
+            ksb, ksh = H_kv * N * D, N * D
+            kpsb, kpsh = kps[0].stride(0), kps[0].stride(1)
+
+            def dense(i, sptr):
+                K, V = caches[i % n_layers]
+                with torch.cuda.stream(torch.cuda.ExternalStream(sptr)):
+                    O.copy_(F.scaled_dot_product_attention(
+                        Qs[i % n_steps][:, :, None], K, V, enable_gqa=True).squeeze(2))
+
+            dense_us = graph_us(dense)
+            for c in SWEEP_C:
+                k = _k_eff(N, c)
+                ws_n = workspace_bytes(B, H, H_kv, N, k)
+                ws = torch.empty(ws_n, dtype=torch.uint8, device=dev)
+
+                def prefix(n):
+                    def run(i, sptr):
+                        K, V = caches[i % n_layers]
+                        st = lib.dcr_decode_prefix(
+                            Qs[i % n_steps].data_ptr(), K.data_ptr(), V.data_ptr(), dcode, ksb,
+                            ksh, ksb, ksh, B, H, H_kv, N, D, k, 1e-12, O.data_ptr(),
+                            ws.data_ptr(), ws_n, sptr, n)
+                        if st:
+                            raise _lib.DCRError(st, "dcr_decode_prefix")
+                    return run
+
+                def proj(i, sptr):
+                    K, V = caches[i % n_layers]
+                    st = lib.dcr_decode_projected(
+                        Qs[i % n_steps].data_ptr(), K.data_ptr(), V.data_ptr(),
+                        kps[i % n_layers].data_ptr(), dcode, ksb, ksh, ksb, ksh, kpsb, kpsh,
+                        Pd.data_ptr(), 16, None, B, H, H_kv, N, D, k, 1e-12, O.data_ptr(),
+                        ws.data_ptr(), ws_n, sptr)
+                    if st:
+                        raise _lib.DCRError(st, "dcr_decode_projected")
+
+                t1 = graph_us(prefix(1))
+                t12 = graph_us(prefix(2))
+                t123 = graph_us(prefix(3))
+                tp = graph_us(proj)
+                # Pass 3's algorithmic bytes: the union of each KV group's selections
+                idx = torch.empty(B * H, k, dtype=torch.int32, device=dev)
+                K0, V0 = caches[0]
+                lib.dcr_select_indices(Qs[0].data_ptr(), K0.data_ptr(), dcode, ksb, ksh, B, H,
+                                       H_kv, N, D, k, 1e-12, idx.data_ptr(), ws.data_ptr(), ws_n,
+                                       stream.cuda_stream)
+                m = torch.zeros(B * H_kv, N, dtype=torch.bool, device=dev)
+                m.view(B, H_kv, N).scatter_(2, idx.view(B, H_kv, (H // H_kv) * k).long(), True)
+                union = int(m.sum())
+                by = [B * H_kv * N * D * 2 + B * H * N * 2,
+                      B * H * N * 2 + B * H * N // 8,
+                      union * 2 * D * 2 + B * H * N // 8 + 2 * B * H * D * 2]
+                us = [t1, t12 - t1, t123 - t12]
+                points.append({
+                    "c": c, "N": N, "B": B, "k_eff": k,
+                    "exact_us": round(t123, 2), "projected_us": round(tp, 2),
+                    "dense_sdpa_us": round(dense_us, 2),
+                    "pass_us": [round(x, 2) for x in us],
+                    "pass_frac_of_hbm": [round(b_ / max(u_, 1e-3) / 1e3 / peak, 3)
+                                         for b_, u_ in zip(by, us)],
+                    "union_rows": union,
+                    "exact_beats_dense": bool(t123 < dense_us),
+                    "projected_beats_dense": bool(tp < dense_us)})
+                del ws, idx, m
+            del caches, kps, Qs
+            torch.cuda.empty_cache()
+    status = _lib.read_device_status(clear=True)
+    return {"points": points, "device_status": status,
+            "method": f"{n_steps} calls per CUDA graph over rotating layer caches (together "
+                      "> 3x L2), CUDA events around the replay; per-pass = marginal times of "
+                      "dcr_decode_prefix(1, 2, 3); Pass 1 bytes = K + scores, Pass 2 = scores "
+                      "+ bitmaps, Pass 3 = union rows x 256 B + bitmaps + Q/O",
+            "dense": "torch.nn.functional.scaled_dot_product_attention(q[B,H,1,D], K, V, "
+                     "enable_gqa=True) on the same fp16 caches",
+            "exact_beats_dense_at": [[p_["c"], p_["N"], p_["B"]] for p_ in points
+                                     if p_["exact_beats_dense"]],
+            "projected_beats_dense_at": [[p_["c"], p_["N"], p_["B"]] for p_ in points
+                                         if p_["projected_beats_dense"]]}
 
 
 def main():
@@ -1037,7 +1263,11 @@ def main():
                     help="skip the 16-layer model decode (config 2) measurement")
     ap.add_argument("--model-steps", type=int, default=64)
     ap.add_argument("--model-tp", action="store_true",
-                    help="instead: config 4 model decode split by KV head over the ranks")
+                    help="instead: only the config 4 model decode split by KV head over the ranks")
+    ap.add_argument("--model-tp-steps", type=int, default=16,
+                    help="timed steps of the config 4 model decode (model_tp in every line)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the config 3 sweep")
+    ap.add_argument("--sweep-steps", type=int, default=20)
     ap.add_argument("--split", choices=["seq", "heads"], default="seq",
                     help="multi-GPU layout: context split by sequence (weak scaling, exact "
                          "global top-K) or KV heads split (strong scaling)")

@@ -22,12 +22,23 @@
 // (0 x inf would reach heads that did not select the row), that warp computes the tile's
 // P.V with scalar fp32 FMAs over each head's own rows instead.
 //
-// The CTAs of a group each write (m, l, o) per head into the workspace partials; the last
-// one (atomic ticket per group, reset by Pass 2 of the next step) merges them into O.
+// The CTAs of a group each write (m, l, o) per head into the workspace partials, laid out
+// group-major ([group][split][head][66]) so that a group's partials are one block; the last
+// CTA (atomic ticket per group, reset by Pass 2 of the next step) merges them into O.
+//
+// The kernel is launched as a programmatic dependent of Pass 2: its CTAs can start while
+// Pass 2's last CTAs drain, load Q, and wait (griddepcontrol.wait) before reading Pass 2's
+// results.
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
 
 namespace dcr {
+
+// Programmatic dependent launch of this kernel behind Pass 2 (compile-time; 0 disables it
+// for comparisons).
+#ifndef DCR_UNION_PDL
+#define DCR_UNION_PDL 1
+#endif
 
 constexpr int kUnThreads = 128;
 constexpr int kUnWarps = kUnThreads / 32;
@@ -45,9 +56,11 @@ struct UnionParams {
   const int32_t* idx;          // [rows][k_eff], every row ascending (when bits is null)
   const uint32_t* bits;        // optional [rows][bits_stride] selection bitmaps from Pass 2
   int64_t bits_stride;
-  int H, H_kv, G, N, k_eff, S, span;
+  int H, H_kv, G, N, k_eff;
+  int S, span;                 // ranges per group and positions per range
+  int S_cap;                   // partial slots per group (the workspace's split capacity)
   void* o;                     // [rows][64]
-  float* part;                 // [rows][S][66]
+  float* part;                 // [groups][S_cap][G][66]
   int* counters;               // [B * H_kv] tickets
 };
 
@@ -139,14 +152,16 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int G = p.G;
-  const int g = blockIdx.x / p.S;  // (b, h_kv)
-  const int s = blockIdx.x - g * p.S;
+  const int S_g = p.S;
+  const int span = p.span;
+  const int g = blockIdx.x / S_g;  // (b, h_kv)
+  const int s = blockIdx.x - g * S_g;
   const int b = g / p.H_kv;
   const int hk = g - b * p.H_kv;
-  const int lo = s * p.span;
-  const int hi = min(p.N, lo + p.span);
+  const int lo = min(p.N, s * span);
+  const int hi = min(p.N, lo + span);
   const int nwords = (hi - lo + 31) >> 5;
-  const int wstride = p.span >> 5;  // words per head in hbits
+  const int wstride = span >> 5;  // words per head in hbits
   const int64_t row0 = static_cast<int64_t>(b) * p.H + static_cast<int64_t>(hk) * G;  // head 0
 
   // ---- Q as the A operand: row r = lane / 4 is head r (rows >= G and 8..15 are zero);
@@ -167,15 +182,25 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
     }
   }
 
+#if DCR_UNION_PDL
+  // launched early behind Pass 2 (programmatic dependent launch): wait for its results
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+
   // ---- the union of the G heads' selections inside [lo, hi): word tid of each head -------
+  // Up to 64 words per range, two threads share a word (16 bits each) so that the list is
+  // emitted by twice as many threads; thread t takes word t >> sh, bits [16 (t & 1), +16).
+  const int sh = nwords <= kUnThreads / 2 ? 1 : 0;
+  const int wi = tid >> sh;
+  const uint32_t part_mask = sh ? (0xffffu << (16 * (tid & 1))) : 0xffffffffu;
   uint32_t hw[kUnMaxG];
 #pragma unroll
   for (int h = 0; h < kUnMaxG; ++h) hw[h] = 0u;
   if (p.bits != nullptr) {  // Pass 2's bitmaps: G loads per thread, all in flight
-    if (tid < nwords) {
+    if (wi < nwords) {
 #pragma unroll
       for (int h = 0; h < kUnMaxG; ++h)
-        if (h < G) hw[h] = __ldg(p.bits + (row0 + h) * p.bits_stride + (lo >> 5) + tid);
+        if (h < G) hw[h] = __ldg(p.bits + (row0 + h) * p.bits_stride + (lo >> 5) + wi);
     }
   } else {  // search each head's ascending index list for the range
   for (int i = tid; i < G * wstride; i += kUnThreads) hbits[i] = 0u;
@@ -229,17 +254,18 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
     }
   }
   __syncthreads();
-  if (tid < nwords) {
+  if (wi < nwords) {
 #pragma unroll
     for (int h = 0; h < kUnMaxG; ++h)
-      if (h < G) hw[h] = hbits[h * wstride + tid];
+      if (h < G) hw[h] = hbits[h * wstride + wi];
   }
   __syncthreads();  // every thread has its words before the ring is reused
   }
-  // a word per thread (span <= 4096 positions)
+  // this thread's share of its word (span <= 4096 positions)
   uint32_t uw = 0u;
 #pragma unroll
   for (int h = 0; h < kUnMaxG; ++h) uw |= hw[h];
+  uw &= part_mask;
   {
     const uint32_t c = __popc(uw);
     const uint32_t incl = warp_incl_scan(c);
@@ -256,7 +282,7 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
       uint32_t heads = 0;
 #pragma unroll
       for (int h = 0; h < kUnMaxG; ++h) heads |= ((hw[h] >> bit) & 1u) << h;
-      list[off++] = un_entry<E>(tid * 32 + bit, heads);
+      list[off++] = un_entry<E>(wi * 32 + bit, heads);
     }
   }
   __syncthreads();  // list complete; the ring is free for the gathers
@@ -443,31 +469,49 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
         acc += sc * (c == 1 ? l_red[w * kUnMaxG + h] : o_red[(w * kUnMaxG + h) * kD + c - 2]);
       }
     }
-    p.part[((row0 + h) * p.S + s) * (kD + 2) + c] = acc;
+    p.part[((static_cast<int64_t>(g) * p.S_cap + s) * G + h) * (kD + 2) + c] = acc;
   }
 
+  const int nparts = S_g;  // partials the group's last CTA merges
+
   // ---- the group's last CTA merges the S partials of each head into O -------------------
-  __threadfence();
+  // The barrier orders every thread's partial stores before thread 0's ticket, an
+  // acquire-release atomic: its release publishes the CTA's partial (cumulative through the
+  // barrier) and, in the last CTA, its acquire makes every other CTA's partial visible to
+  // the loads that follow the next barrier. No separate fences.
   __syncthreads();
-  if (tid == 0) is_last = atomicAdd(p.counters + g, 1) == p.S - 1;
+  if (tid == 0) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;"
+                 : "=r"(old)
+                 : "l"(p.counters + g)
+                 : "memory");
+    is_last = old == S_g - 1;
+  }
   __syncthreads();
   if (!is_last) return;
-  __threadfence();
-  // The group's partials are contiguous ([G rows][S][66] floats): stage them in the ring with
-  // 16-byte loads (up to 12 per thread in flight at once) when they fit, then merge from
-  // shared memory with one scale exp2(m_q - M) per (head, split).
-  const int nfl = G * p.S * (kD + 2);
-  const float* gpart = p.part + row0 * p.S * (kD + 2);
-  // at the end of the ring: scales [kUnMaxG][128] and the heads' maxima [kUnMaxG]
-  constexpr int kScFloats = kUnMaxG * 128 + kUnMaxG;
-  float* sc_s = reinterpret_cast<float*>(ring) + kUnStages * kUnStageBytes / 4 - kScFloats;
-  float* Ms = sc_s + kUnMaxG * 128;
-  const bool staged = (nfl + kScFloats) * 4 <= kUnStages * kUnStageBytes && p.S <= 128;
-  if (staged) {
-    float* sp = reinterpret_cast<float*>(ring);
+  // The group's partials are one block ([nparts][G][66] floats). They are staged in the ring
+  // in chunks of up to `cap` splits (16-byte loads, up to 12 per thread in flight), and every
+  // output folds a chunk into its running (M, L, o) online: item = (head, pair of dims), `tpi`
+  // adjacent lanes per item, each taking every tpi-th split of the chunk, combined by
+  // shuffles at the end.
+  const int qs = G * (kD + 2);  // floats between consecutive splits of one head
+  const float* gpart = p.part + static_cast<int64_t>(g) * p.S_cap * qs;
+  const int cap = kUnStages * kUnStageBytes / 4 / qs;
+  float* sp = reinterpret_cast<float*>(ring);
+  const int items = G * (kD / 2);
+  const int tpi = items >= kUnThreads ? 1 : kUnThreads / items;  // G = 1, 2, 4, 8: 4, 2, 1, 1
+  const int rounds = (items * tpi + kUnThreads - 1) / kUnThreads;  // 2 for G = 8, else 1
+  float Mr[2] = {-INFINITY, -INFINITY}, Lr[2] = {0.0f, 0.0f};
+  float2 Ar[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+  for (int q0 = 0; q0 < nparts; q0 += cap) {
+    const int cnt = min(cap, nparts - q0);
+    const int nfl = cnt * qs;
+    const float* src = gpart + static_cast<int64_t>(q0) * qs;
+    if (q0 > 0) __syncthreads();  // the previous chunk is consumed
     int done = 0;
-    if ((reinterpret_cast<uintptr_t>(gpart) & 15u) == 0) {  // 264-byte splits: not always
-      const float4* src4 = reinterpret_cast<const float4*>(gpart);
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {  // 264-byte splits: not always
+      const float4* src4 = reinterpret_cast<const float4*>(src);
       float4* dst4 = reinterpret_cast<float4*>(sp);
       const int n4 = nfl / 4;
       for (int i0 = 0; i0 < n4; i0 += 12 * kUnThreads) {
@@ -490,7 +534,7 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int i = i0 + u * kUnThreads + tid;
-        if (i < nfl) v[u] = __ldcg(gpart + i);
+        if (i < nfl) v[u] = __ldcg(src + i);
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
@@ -499,49 +543,59 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
       }
     }
     __syncthreads();
-    // per (head, split) scales: thread h < G finds the head's maximum, then the scales
-    if (tid < G) {
-      float M = -INFINITY;
-      for (int q = 0; q < p.S; ++q) M = fmaxf(M, sp[(tid * p.S + q) * (kD + 2)]);
-      Ms[tid] = M;
-    }
-    __syncthreads();
-    for (int i = tid; i < G * p.S; i += kUnThreads) {
-      const int h = i / p.S;
-      const float mq = sp[i * (kD + 2)];
-      sc_s[h * 128 + (i - h * p.S)] = mq == -INFINITY ? 0.0f : exp2f(mq - Ms[h]);
-    }
-    __syncthreads();
-    for (int i = tid; i < G * kD; i += kUnThreads) {
-      const int h = i / kD, d = i - h * kD;
-      const float* pr = sp + h * p.S * (kD + 2);
-      const float* sch = sc_s + h * 128;
-      float L = 0.0f, acc = 0.0f;
-      for (int q = 0; q < p.S; ++q) {
-        L = fmaf(sch[q], pr[q * (kD + 2) + 1], L);
-        acc = fmaf(sch[q], pr[q * (kD + 2) + 2 + d], acc);
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      if (rr >= rounds) break;
+      const int item = (rr * kUnThreads + tid) / tpi;
+      if (item >= items) continue;
+      const int part = (rr * kUnThreads + tid) - item * tpi;
+      const int h = item / (kD / 2), dp = item - h * (kD / 2);
+      const float* pr = sp + h * (kD + 2);
+      // the head's maximum over the chunk (the same splits for every lane of the head)
+      float Mc = -INFINITY;
+#pragma unroll 4
+      for (int q = 0; q < cnt; ++q) Mc = fmaxf(Mc, pr[q * qs]);
+      const float Mn = fmaxf(Mr[rr], Mc);
+      if (Mn == -INFINITY) continue;  // nothing selected so far
+      const float a = Mr[rr] == -INFINITY ? 0.0f : exp2f(Mr[rr] - Mn);
+      float L = Lr[rr] * a;
+      float2 A = make_float2(Ar[rr].x * a, Ar[rr].y * a);
+#pragma unroll 4
+      for (int q = part; q < cnt; q += tpi) {
+        const float mq = pr[q * qs];
+        const float sc = mq == -INFINITY ? 0.0f : exp2f(mq - Mn);
+        const float2 ov = *reinterpret_cast<const float2*>(pr + q * qs + 2 + 2 * dp);
+        L = fmaf(sc, pr[q * qs + 1], L);
+        A.x = fmaf(sc, ov.x, A.x);
+        A.y = fmaf(sc, ov.y, A.y);
       }
-      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + d), acc / L);
+      Mr[rr] = Mn;
+      Lr[rr] = L;
+      Ar[rr] = A;
     }
-  } else {
-    for (int i = tid; i < G * kD; i += kUnThreads) {
-      const int h = i / kD, d = i - h * kD;
-      const float* pr = gpart + h * p.S * (kD + 2);
-      float M = -INFINITY;
-      for (int q = 0; q < p.S; ++q) M = fmaxf(M, __ldcg(pr + q * (kD + 2)));
-      float L = 0.0f, acc = 0.0f;
-      for (int q = 0; q < p.S; ++q) {
-        const float* e = pr + q * (kD + 2);
-        const float mq = __ldcg(e);
-        const float sc = mq == -INFINITY ? 0.0f : exp2f(mq - M);
-        L += sc * __ldcg(e + 1);
-        acc += sc * __ldcg(e + 2 + d);
-      }
-      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + d), acc / L);
+  }
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    if (rr >= rounds) break;
+    const int item = (rr * kUnThreads + tid) / tpi;
+    const int part = (rr * kUnThreads + tid) - item * tpi;
+    float L = Lr[rr];
+    float2 A = Ar[rr];
+    for (int o2 = 1; o2 < tpi; o2 <<= 1) {  // lanes of an item share Mr: plain sums
+      L += __shfl_xor_sync(0xffffffffu, L, o2);
+      A.x += __shfl_xor_sync(0xffffffffu, A.x, o2);
+      A.y += __shfl_xor_sync(0xffffffffu, A.y, o2);
+    }
+    if (item < items && part == 0) {
+      const int h = item / (kD / 2), dp = item - h * (kD / 2);
+      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp), A.x / L);
+      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
     }
   }
   if (tid == 0) p.counters[g] = 0;
 }
+
+constexpr int kUnSpanMin = 256;
 
 int union_max_splits(int N) {
   const int min_s = (N + kUnSpanMax - 1) / kUnSpanMax;
@@ -557,6 +611,10 @@ static void union_split(int N, int groups, int per_sm, int& S, int& span) {
   const int min_s = (N + kUnSpanMax - 1) / kUnSpanMax;
   if (S < min_s) S = min_s;
   if (S > union_max_splits(N)) S = union_max_splits(N);  // what the workspace partials hold
+  // at least kUnSpanMin positions per range: below that a CTA's fixed costs (list, partial,
+  // ticket) outweigh its gathers
+  const int max_s = (N + kUnSpanMin - 1) / kUnSpanMin;
+  if (S > max_s && max_s >= min_s) S = max_s;
   span = ((N + S - 1) / S + 31) / 32 * 32;
   if (span > kUnSpanMax) span = kUnSpanMax;
   S = (N + span - 1) / span;
@@ -565,6 +623,7 @@ static void union_split(int N, int groups, int per_sm, int& S, int& span) {
 template <typename T, typename E>
 static int launch_union_t(UnionParams p, int groups, int part_splits, cudaStream_t st) {
   const void* fn = reinterpret_cast<const void*>(&attend_union_kernel<T, E>);
+  p.S_cap = part_splits;
   if (ensure_smem_attr(fn, union_smem_bytes(kUnSpanMax, sizeof(E))) != cudaSuccess)
     return DCR_ERR_CUDA;
   // size the split for 4 CTAs per SM, then for what the resulting shared memory allows
@@ -579,9 +638,19 @@ static int launch_union_t(UnionParams p, int groups, int part_splits, cudaStream
   if (p.S > part_splits) return DCR_ERR_SHAPE;
   const int64_t grid = static_cast<int64_t>(groups) * p.S;
   if (grid <= 0 || grid > 0x7fffffff) return DCR_ERR_SHAPE;
-  attend_union_kernel<T, E><<<static_cast<unsigned>(grid), kUnThreads,
-                              union_smem_bytes(p.span, sizeof(E)), st>>>(p);
-  return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
+  // launched as a programmatic dependent of the preceding kernel (Pass 2)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kUnThreads);
+  cfg.dynamicSmemBytes = union_smem_bytes(p.span, sizeof(E));
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = DCR_UNION_PDL ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, attend_union_kernel<T, E>, p) == cudaSuccess ? DCR_OK
+                                                                               : DCR_ERR_CUDA;
 }
 
 // The decode steps use the union Pass 3 for 16-bit caches; DCR_ATTEND_UNION=0 in the

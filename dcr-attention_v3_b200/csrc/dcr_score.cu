@@ -11,8 +11,9 @@
 // caches) with G = H / H_kv query heads scored per row. A persistent grid of
 // 3 CTAs per SM (for 16-bit caches and G = 4; the count follows the shared-memory size)
 // walks contiguous ranges of 256-row tiles; one thread per CTA issues 4-D TMA tile loads
-// (128-byte swizzle) into a 2-stage shared-memory ring completed by mbarriers. Every thread scores two rows of each tile (r and r + 128) with packed fp32
-// FMAs (fma.rn.f32x2) that advance two heads of one row per instruction: the unit
+// (128-byte swizzle) into a 2-stage shared-memory ring completed by mbarriers. Every
+// thread scores two rows of each tile (r and r + 128) with packed fp32 FMAs
+// (fma.rn.f32x2) that advance two heads of one row per instruction: the unit
 // queries sit in shared memory transposed, u_t[d][head], so one 16-byte load feeds two
 // head pairs. (For G = 1 the pair is two rows of one head and u is stored as {u, u}.)
 // Each lane of the packed FMA is an IEEE fma, so the fp32 dot product of every

@@ -35,6 +35,10 @@
 
 namespace cg = cooperative_groups;
 
+#ifndef DCR_UNION_PDL
+#define DCR_UNION_PDL 1
+#endif
+
 namespace dcr {
 
 #ifndef DCR_P2_WIDE
@@ -115,6 +119,10 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
       __syncthreads();
   };
 
+#if DCR_UNION_PDL
+  // let the union Pass 3 launch now; it waits for this grid before reading its results
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
   if (crank == 0 && tid == 0 && p.row_counters != nullptr) p.row_counters[row] = 0;
   if (tid == 0) {
     s_bh = 0;
