@@ -31,6 +31,7 @@
 // results.
 #include "dcr_common.cuh"
 #include "dcr_internal.h"
+#include "dcr_peer.cuh"
 
 namespace dcr {
 
@@ -59,7 +60,10 @@ struct UnionParams {
   int H, H_kv, G, N, k_eff;
   int S, span;                 // ranges per group and positions per range
   int S_cap;                   // partial slots per group (the workspace's split capacity)
-  void* o;                     // [rows][64]
+  void* o;                     // [rows][64] (when state is null)
+  float* state;                // optional [rows][66]: unnormalised (m, l, o) instead of O,
+  PeerView pv;                 // or, with pv.world > 0, published into the ranks' exchange
+                               // buffers (the sequence-sharded step's state exchange)
   float* part;                 // [groups][S_cap][G][66]
   int* counters;               // [B * H_kv] tickets
 };
@@ -588,8 +592,29 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
     }
     if (item < items && part == 0) {
       const int h = item / (kD / 2), dp = item - h * (kD / 2);
-      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp), A.x / L);
-      ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
+      if (p.state == nullptr) {
+        ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp), A.x / L);
+        ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
+      } else if (p.pv.world > 0) {  // epoch-tagged words into slot `rank` of every rank
+        const uint32_t epoch = step_epoch(p.pv);
+        for (int q = 0; q < p.pv.world; ++q) {
+          uint64_t* dst = p.pv.st(q, p.pv.rank, row0 + h);
+          ll_put(dst + 2 + 2 * dp, __float_as_uint(A.x), epoch);
+          ll_put(dst + 3 + 2 * dp, __float_as_uint(A.y), epoch);
+          if (dp == 0) {
+            ll_put(dst, __float_as_uint(Mr[rr]), epoch);
+            ll_put(dst + 1, __float_as_uint(L), epoch);
+          }
+        }
+      } else {
+        float* st = p.state + (row0 + h) * (kD + 2);
+        st[2 + 2 * dp] = A.x;
+        st[3 + 2 * dp] = A.y;
+        if (dp == 0) {
+          st[0] = Mr[rr];
+          st[1] = L;
+        }
+      }
     }
   }
   if (tid == 0) p.counters[g] = 0;
@@ -674,9 +699,12 @@ int launch_attend_union(const void* Q, const void* K, const void* V, int dtype, 
                         int64_t ksh, int64_t vsb, int64_t vsh, const int32_t* idx,
                         const uint32_t* bits, int64_t bits_stride, int B, int H, int H_kv, int N,
                         int k_eff, void* O, float* partials, int part_splits, int* counters,
-                        cudaStream_t st) {
+                        cudaStream_t st, float* state, const PeerView* pv) {
   if (!union_supported(dtype, H, H_kv)) return DCR_ERR_SHAPE;
   UnionParams p;
+  p.state = state;
+  p.pv.world = 0;
+  if (pv != nullptr && state != nullptr) p.pv = *pv;
   p.q = Q;
   p.k = K;
   p.v = V;

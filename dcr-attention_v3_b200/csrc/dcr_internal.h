@@ -64,7 +64,8 @@ int launch_attend_union(const void* Q, const void* K, const void* V, int dtype, 
                         int64_t ksh, int64_t vsb, int64_t vsh, const int32_t* idx,
                         const uint32_t* bits, int64_t bits_stride, int B, int H, int H_kv, int N,
                         int k_eff, void* O, float* partials, int part_splits, int* counters,
-                        cudaStream_t st);
+                        cudaStream_t st, float* state = nullptr,
+                        const struct PeerView* pv = nullptr);
 
 // Workspace layout shared by dcr_decode / dcr_select_indices / dcr_attend.
 struct WorkspaceLayout {
@@ -115,8 +116,11 @@ struct ShardLayout {
   size_t count;      // int32 [rows]
   size_t row_state;  // int32 [rows * 4]
   size_t chunk_cnt;  // uint32 [rows * chunks]
+  size_t bits;       // uint32 [rows * bits_stride] selection bitmaps (fused selection)
+  int64_t bits_stride;
   size_t total;
   int splits, cap, chunks;
+  int part_splits;   // splits the partials hold (the union Pass 3 may use more)
   int64_t n_pad;
 };
 ShardLayout shard_layout(int rows, int N_local, int k_eff);
@@ -138,9 +142,11 @@ int launch_shard_combine(const float* states, int world, int rows, int dtype, vo
 // per row (n_local_max, the longest chunk of all ranks, <= 32768: every rank decides
 // alike); *launched tells whether it ran. DCR_ERR_SHAPE if the rows cannot all be
 // resident (every rank, same GPUs, fails alike).
+// *bits_written: the selection was also written as bitmaps (w.bits; every thread's
+// positions are whole 32-bit words), which the union Pass 3 reads.
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
                               int n_local_max, int k_eff, const struct PeerView* pv,
-                              cudaStream_t st, bool* launched);
+                              cudaStream_t st, bool* launched, bool* bits_written = nullptr);
 
 // Projected-score mode (dcr_project.cu). Append: copies n_new rows of K and V into the
 // caches at position pos (k_cache may be null: no copy) and writes their projection

@@ -126,8 +126,9 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
                          reinterpret_cast<uint16_t*>(ws + w.scores), w.n_pad, 1, s)))
     return st;
   if ((st = mark(1))) return st;
-  bool fused = false;
-  if ((st = launch_shard_select_fused(w, ws, rows, N_local, n_local_max, k_eff, &v, s, &fused)))
+  bool fused = false, bits = false;
+  if ((st = launch_shard_select_fused(w, ws, rows, N_local, n_local_max, k_eff, &v, s, &fused,
+                                      &bits)))
     return st;
   if (fused) {
     if ((st = mark(2)) || (st = mark(3))) return st;
@@ -145,7 +146,16 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
   // Pass 3 publishes its states into the exchange buffers; the pointer only selects the
   // state output
   float* own_state = reinterpret_cast<float*>(v.base[rank] + v.lay.st);
-  if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+  if (fused && bits && union_enabled() && union_supported(dtype, H, H_kv)) {
+    // the union Pass 3 over the fused selection's bitmaps
+    if ((st = launch_attend_union(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
+                                  reinterpret_cast<const int32_t*>(ws + w.idx),
+                                  reinterpret_cast<const uint32_t*>(ws + w.bits), w.bits_stride,
+                                  B, H, H_kv, N_local, w.cap, nullptr,
+                                  reinterpret_cast<float*>(ws + w.partials), w.part_splits,
+                                  reinterpret_cast<int*>(ws + w.counters), s, own_state, &v)))
+      return st;
+  } else if ((st = launch_attend(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
                           reinterpret_cast<const int32_t*>(ws + w.idx),
                           reinterpret_cast<const int32_t*>(ws + w.count), B, H, H_kv, N_local,
                           w.cap, nullptr, own_state, w.splits,

@@ -58,6 +58,8 @@ struct ShardParams {
   int* counters;              // Pass 3 split-K tickets, reset by phase 3
   PeerView v;                 // v.world > 0: exchange through the peers' buffers instead of
                               // hist_hi / hist_out / hist_lo_all
+  uint32_t* bits;             // optional (fused selection): [rows][bits_stride] bitmaps of the
+  int64_t bits_stride;        // selected local positions, written besides idx
 };
 
 // The 32 keys of this thread in chunk `chunk` of row `row`; 0 past the end of the row
@@ -558,6 +560,9 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
       sel |= eq & ~rem;
       take = 0;
     }
+    // whole words (VPT a multiple of 4: positions base + 32 w start a word)
+    if (p.bits != nullptr && base + 32 * w < p.N)
+      p.bits[row * p.bits_stride + ((base + 32 * w) >> 5)] = sel;
     while (sel) {
       const int bb = __ffs(sel) - 1;
       sel &= sel - 1;
@@ -584,7 +589,10 @@ ShardLayout shard_layout(int rows, int N_local, int k_eff) {
   w.counters = off;
   off = align_up_256(off + sizeof(int) * static_cast<size_t>(rows));
   w.partials = off;
-  off = align_up_256(off + sizeof(float) * static_cast<size_t>(rows) * w.splits * (kD + 2));
+  w.part_splits = w.splits;
+  if (union_enabled() && union_max_splits(N_local) > w.part_splits)
+    w.part_splits = union_max_splits(N_local);
+  off = align_up_256(off + sizeof(float) * static_cast<size_t>(rows) * w.part_splits * (kD + 2));
   w.scores = off;
   off = align_up_256(off + sizeof(uint16_t) * static_cast<size_t>(rows) * w.n_pad);
   w.idx = off;
@@ -595,6 +603,9 @@ ShardLayout shard_layout(int rows, int N_local, int k_eff) {
   off = align_up_256(off + sizeof(int32_t) * 4 * static_cast<size_t>(rows));
   w.chunk_cnt = off;
   off = align_up_256(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.chunks);
+  w.bits = off;
+  w.bits_stride = (static_cast<int64_t>(N_local) + 31) / 32;
+  off = align_up_256(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.bits_stride);
   w.total = off;
   return w;
 }
@@ -615,6 +626,8 @@ static ShardParams shard_params(const ShardLayout& w, uint8_t* ws, int rows, int
   p.idx = reinterpret_cast<int32_t*>(ws + w.idx);
   p.count = reinterpret_cast<int32_t*>(ws + w.count);
   p.counters = reinterpret_cast<int*>(ws + w.counters);
+  p.bits = nullptr;
+  p.bits_stride = w.bits_stride;
   return p;
 }
 
@@ -680,8 +693,9 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
 
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
                               int n_local_max, int k_eff, const PeerView* pv, cudaStream_t st,
-                              bool* launched) {
+                              bool* launched, bool* bits_written) {
   *launched = false;
+  if (bits_written != nullptr) *bits_written = false;
   // every rank takes the same path: decided from the longest chunk of all ranks
   if (pv == nullptr || n_local_max > kFsThreads * 64 || N_local > n_local_max) return DCR_OK;
   const int nvec = (N_local + 7) / 8;
@@ -692,6 +706,11 @@ int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N
   const int vpt = (nvec + kFsThreads - 1) / kFsThreads;
   if (vpt <= 1) return launch_fused_t<1>(p, st, launched);
   if (vpt <= 2) return launch_fused_t<2>(p, st, launched);
+  // 4 or 8 vectors per thread: whole 32-bit words, so the bitmaps go out too
+  if (bits_written != nullptr) {
+    p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
+    *bits_written = true;
+  }
   if (vpt <= 4) return launch_fused_t<4>(p, st, launched);
   return launch_fused_t<8>(p, st, launched);
 }
