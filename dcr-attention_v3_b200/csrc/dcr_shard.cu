@@ -381,8 +381,7 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
 // waits only for the same row of the other ranks, never for another CTA of its own GPU;
 // the kernel runs only when all its rows fit in one wave (every rank alike), so no row
 // waits behind a row that the other GPU has not started.
-constexpr int kFsThreads = 512;
-constexpr int kFsWarps = kFsThreads / 32;
+constexpr int kFsThreads = 512;  // CTA size for chunks up to 8192 positions (else 1024)
 
 // Publishes this row's 256-bin histogram h (exchange x, packed words) into slot `rank` of
 // every rank's buffer and sums every rank's row into out. Block-wide; ends with a barrier.
@@ -413,13 +412,14 @@ __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, in
   __syncthreads();
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const ShardParams p) {
+template <int VPT, int TPB>
+__global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardParams p) {
   constexpr int kKeys = VPT * 8;
   constexpr int kWords = (kKeys + 31) / 32;
+  constexpr int kWarpsB = TPB / 32;
   __shared__ uint32_t hist[256];
   __shared__ uint32_t hsum[256];
-  __shared__ uint32_t wsum[kFsWarps];
+  __shared__ uint32_t wsum[kWarpsB];
   __shared__ uint32_t s_bh, s_above, s_T, s_quota, s_tot;
   const PeerView& v = p.v;
   const int tid = threadIdx.x;
@@ -534,10 +534,10 @@ __global__ void __launch_bounds__(kFsThreads, 1) shard_select_fused_kernel(const
   if (lane == 31) wsum[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const uint32_t ws = lane < kFsWarps ? wsum[lane] : 0u;
+    const uint32_t ws = lane < kWarpsB ? wsum[lane] : 0u;
     const uint32_t wi = warp_incl_scan(ws);
-    if (lane < kFsWarps) wsum[lane] = wi - ws;
-    if (lane == kFsWarps - 1) s_tot = wi;
+    if (lane < kWarpsB) wsum[lane] = wi - ws;
+    if (lane == kWarpsB - 1) s_tot = wi;
   }
   __syncthreads();
   const uint32_t ex = incl - packed + wsum[warp];
@@ -671,21 +671,21 @@ int launch_shard_select(const ShardLayout& w, uint8_t* ws, int rows, int N_local
   return check_launch();
 }
 
-template <int VPT>
+template <int VPT, int TPB>
 static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched) {
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, shard_select_fused_kernel<VPT>,
-                                                    kFsThreads, 0) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, shard_select_fused_kernel<VPT, TPB>,
+                                                    TPB, 0) != cudaSuccess)
     return DCR_ERR_CUDA;
   if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_ERR_SHAPE;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.rows));
-  cfg.blockDim = dim3(kFsThreads);
+  cfg.blockDim = dim3(TPB);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cfg.attrs = nullptr;
   cfg.numAttrs = 0;
-  if (cudaLaunchKernelEx(&cfg, shard_select_fused_kernel<VPT>, p) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, shard_select_fused_kernel<VPT, TPB>, p) != cudaSuccess)
     return DCR_ERR_CUDA;
   *launched = true;
   return DCR_OK;
@@ -703,16 +703,30 @@ int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N
   p.v = *pv;
   p.world = pv->world;
   p.rank = pv->rank;
+  // Past 8192 positions, when every row has its own SM: 1024-thread CTAs with at most 32
+  // keys per thread (Pass 2's launch shape there); otherwise 512 threads with up to 64.
+  // The shape follows n_local_max and rows, the same on every rank.
+  const int nvec_max = (n_local_max + 7) / 8;
+  if (nvec_max > 512 * 2 && rows <= device_sm_count()) {
+    const int vpt = (nvec + 1023) / 1024;
+    if (vpt <= 2) return launch_fused_t<2, 1024>(p, st, launched);
+    // 4 vectors per thread: whole 32-bit words, so the bitmaps go out too
+    if (bits_written != nullptr) {
+      p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
+      *bits_written = true;
+    }
+    return launch_fused_t<4, 1024>(p, st, launched);
+  }
   const int vpt = (nvec + kFsThreads - 1) / kFsThreads;
-  if (vpt <= 1) return launch_fused_t<1>(p, st, launched);
-  if (vpt <= 2) return launch_fused_t<2>(p, st, launched);
+  if (vpt <= 1) return launch_fused_t<1, kFsThreads>(p, st, launched);
+  if (vpt <= 2) return launch_fused_t<2, kFsThreads>(p, st, launched);
   // 4 or 8 vectors per thread: whole 32-bit words, so the bitmaps go out too
   if (bits_written != nullptr) {
     p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
     *bits_written = true;
   }
-  if (vpt <= 4) return launch_fused_t<4>(p, st, launched);
-  return launch_fused_t<8>(p, st, launched);
+  if (vpt <= 4) return launch_fused_t<4, kFsThreads>(p, st, launched);
+  return launch_fused_t<8, kFsThreads>(p, st, launched);
 }
 
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
