@@ -744,6 +744,17 @@ def model_decode_bench(dev, n_steps, stream):
     }
 
 
+def _limiting_phase(split):
+    """The longest phase of a per-phase split of the sharded step (or None)."""
+    if not split:
+        return None
+    name = max(split, key=lambda n: split[n])
+    return {"phase": name, "us": split[name],
+            "note": "longest phase of the per-kernel split above (CUDA events between the "
+                    "kernels inside one graph; each event node adds a few microseconds, and "
+                    "a phase that waits on the other ranks includes their skew)"}
+
+
 def run_sharded_arm(args):
     """N > 1: one layer-step over a KV cache split across the ranks (one GPU each).
 
@@ -994,6 +1005,7 @@ def run_sharded_arm(args):
                    "clock_soak_s": args.soak},
         "nccl_phases_us": phases,
         "peer_kernels_us": peer_kernels,
+        "limiting_phase": _limiting_phase(peer_kernels if peer_kernels else phases),
         "cpu_baseline": None,
         "e2e": {"value": round(e2e_ms * 1e3 / steps, 3), "unit": UNIT,
                 "h2d_bytes_per_step": B * H * D * eb, "d2h_bytes_per_step": B * H * D * eb,
