@@ -761,8 +761,9 @@ def run_sharded_arm(args):
     --split seq (default): rank r holds positions [32768 r, 32768 (r+1)) of every cache
     row of the hero layer (B=4, 32/8 heads), so the whole job is a layer-step over an
     N = 32768 * world context with k_eff = adaptive_k_window(64, N, 0.15); the exact global
-    top-K takes two histogram exchanges and the outputs one (m, l, o) exchange (NCCL).
-    Weak scaling: the per-GPU work stays that of the 1-GPU hero step.
+    top-K takes two histogram exchanges and the outputs one (m, l, o) exchange, pushed by
+    the kernels into the peers' buffers (--exchange peer, default) or as NCCL collectives
+    (--exchange nccl). Weak scaling: the per-GPU work stays that of the 1-GPU hero step.
     --split heads: the hero layer's 8 KV heads split over the ranks and one all-gather of
     O (strong scaling)."""
     import torch
@@ -984,9 +985,16 @@ def run_sharded_arm(args):
     model_tp = None
     if not args.no_model and H_kv % world == 0:
         model_tp = _model_tp_safe(dev, world, rank, args.model_tp_steps)
-    # our kernels per step; seq: score, 2 histograms, count, emit, attend, combine;
-    # heads: the 3 passes of dcr_decode
-    launches_per_step = 7 if seq else 3
+    # our kernels per step. seq over NCCL: score, 2 histograms, count, emit, attend, combine;
+    # seq over peer memory: score, the fused selection (chunks up to 32768 positions, every
+    # row resident: the bench's 128 rows always are), Pass 3, combine -- else score,
+    # 2 histograms, selection, Pass 3, combine; heads: the 3 passes of dcr_decode
+    if not seq:
+        launches_per_step = 3
+    elif args.exchange != "peer":
+        launches_per_step = 7
+    else:
+        launches_per_step = 4 if n_local <= 32768 else 6
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(ms / steps, 5),

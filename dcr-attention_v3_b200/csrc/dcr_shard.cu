@@ -677,7 +677,10 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, shard_select_fused_kernel<VPT, TPB>,
                                                     TPB, 0) != cudaSuccess)
     return DCR_ERR_CUDA;
-  if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_ERR_SHAPE;
+  // Every row's CTA waits on the same row of the other ranks, so all rows must be resident
+  // at once; otherwise the caller runs the phase kernels (rows and the launch shape are the
+  // same on every rank, so every rank decides alike).
+  if (static_cast<int64_t>(per_sm) * device_sm_count() < p.rows) return DCR_OK;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.rows));
   cfg.blockDim = dim3(TPB);
@@ -707,26 +710,29 @@ int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N
   // keys per thread (Pass 2's launch shape there); otherwise 512 threads with up to 64.
   // The shape follows n_local_max and rows, the same on every rank.
   const int nvec_max = (n_local_max + 7) / 8;
+  // With 4 or 8 vectors per thread a thread's keys are whole 32-bit words, so the bitmaps
+  // go out too.
+  auto with_bits = [&](int e) {
+    if (bits_written != nullptr) *bits_written = e == DCR_OK && *launched;
+    return e;
+  };
+  if (bits_written != nullptr) p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
   if (nvec_max > 512 * 2 && rows <= device_sm_count()) {
     const int vpt = (nvec + 1023) / 1024;
-    if (vpt <= 2) return launch_fused_t<2, 1024>(p, st, launched);
-    // 4 vectors per thread: whole 32-bit words, so the bitmaps go out too
-    if (bits_written != nullptr) {
-      p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
-      *bits_written = true;
+    if (vpt <= 2) {
+      p.bits = nullptr;
+      return launch_fused_t<2, 1024>(p, st, launched);
     }
-    return launch_fused_t<4, 1024>(p, st, launched);
+    return with_bits(launch_fused_t<4, 1024>(p, st, launched));
   }
   const int vpt = (nvec + kFsThreads - 1) / kFsThreads;
-  if (vpt <= 1) return launch_fused_t<1, kFsThreads>(p, st, launched);
-  if (vpt <= 2) return launch_fused_t<2, kFsThreads>(p, st, launched);
-  // 4 or 8 vectors per thread: whole 32-bit words, so the bitmaps go out too
-  if (bits_written != nullptr) {
-    p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
-    *bits_written = true;
+  if (vpt <= 2) {
+    p.bits = nullptr;
+    return vpt <= 1 ? launch_fused_t<1, kFsThreads>(p, st, launched)
+                    : launch_fused_t<2, kFsThreads>(p, st, launched);
   }
-  if (vpt <= 4) return launch_fused_t<4, kFsThreads>(p, st, launched);
-  return launch_fused_t<8, kFsThreads>(p, st, launched);
+  if (vpt <= 4) return with_bits(launch_fused_t<4, kFsThreads>(p, st, launched));
+  return with_bits(launch_fused_t<8, kFsThreads>(p, st, launched));
 }
 
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,

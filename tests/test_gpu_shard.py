@@ -169,17 +169,19 @@ class _OneRank:
         pass
 
 
-@pytest.mark.parametrize("N,k", [(5000, 750), (20000, 3000)])
-def test_peer_exchange_single_rank_steps(oracle_mod, cuda_lib, N, k):
-    """The peer-exchange step with one rank: every kernel of the fused path (no peer to
-    wait for), over consecutive steps (the epoch advances), eager and as a graph replay.
+@pytest.mark.parametrize("B,N,k", [(2, 5000, 750), (2, 20000, 3000), (24, 5000, 750)])
+def test_peer_exchange_single_rank_steps(oracle_mod, cuda_lib, B, N, k):
+    """The peer-exchange step with one rank: every kernel of the path (no peer to wait
+    for), over consecutive steps (the epoch advances), eager and as a graph replay.
     N=5000 gives the fused selection 2 vectors of keys per thread (index lists, the
     per-head Pass 3); N=20000 gives it whole 32-bit words per thread, so it also writes
-    bitmaps and the step runs the union Pass 3 with its state published into the buffer."""
+    bitmaps and the step runs the union Pass 3 with its state published into the buffer.
+    B=24 gives 768 rows, more than one wave of the fused selection's CTAs, so the step
+    runs the phase kernels (histograms, selection) with the same exchanges."""
     from dcr_b200 import _lib
     from dcr_b200.sharded import SequenceShardedDecoder
     from dcr_b200.synthetic import fresh_queries, make_decode_inputs
-    B, H, H_kv = 2, 32, 8
+    H, H_kv = 32, 8
     _, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.bfloat16, seed=4)
     Qs = fresh_queries(4, B, H, dtype=torch.bfloat16, seed=6)
     Kd, Vd = K.to(DEV), V.to(DEV)
