@@ -3,6 +3,7 @@
 // them as one unit keeps that a plain __device__ variable without relocatable device code.
 #include "dcr_score.cu"
 #include "dcr_select.cu"
+#include "dcr_select_stream.cu"
 #include "dcr_attend.cu"
 #include "dcr_attend_union.cu"
 #include "dcr_shard.cu"

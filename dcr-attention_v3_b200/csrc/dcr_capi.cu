@@ -69,6 +69,9 @@ WorkspaceLayout workspace_layout(int rows, int N, int k_eff) {
     w.bits_stride = (static_cast<int64_t>(N) + 31) / 32;
     off = align_up(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.bits_stride, 256);
   }
+  w.sel = off;
+  w.sel_bytes = select_stream_bytes(rows, N);
+  off = align_up(off + w.sel_bytes, 256);
   w.total = off;
   return w;
 }
@@ -202,6 +205,27 @@ int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, in
                        static_cast<cudaStream_t>(stream));
 }
 
+size_t dcr_select_workspace_bytes(int rows, int N) {
+  if (rows <= 0 || N <= 0) return 0;
+  return select_stream_bytes(rows, N);
+}
+
+int dcr_select_ws(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+                  int32_t* idx_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (scores == nullptr || idx_out == nullptr) return DCR_ERR_NULL;
+  if (rows <= 0 || N <= 0 || s_stride_row < N) return DCR_ERR_SHAPE;
+  int st = check_k(k_eff, N);
+  if (st) return st;
+  const size_t need = select_stream_bytes(rows, N);
+  if (need > 0) {
+    if (workspace == nullptr || workspace_bytes < need) return DCR_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return DCR_ERR_ALIGN;
+  }
+  return launch_select(scores, s_stride_row, rows, N, k_eff, 0, idx_out, nullptr,
+                       static_cast<cudaStream_t>(stream), nullptr, 0, nullptr,
+                       need > 0 ? static_cast<uint8_t*>(workspace) : nullptr);
+}
+
 int dcr_attend(const void* Q, const void* K, const void* V, int dtype, int64_t k_stride_b,
                int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_h, const int32_t* idx,
                int B, int H, int H_kv, int N, int D, int k_eff, void* O, void* workspace,
@@ -251,7 +275,8 @@ int dcr_select_indices(const void* Q, const void* K, int dtype, int64_t k_stride
   if ((st = launch_score(K, dtype, k_stride_b, k_stride_h, nullptr, Q, eps, B, H, H_kv, N, scores,
                          w.n_pad, 1, s)))
     return st;
-  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
+  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s, nullptr, 0,
+                       nullptr, w.sel_bytes ? ws + w.sel : nullptr);
 }
 
 // Projected-score inputs of a decode step (null kp: the exact Pass 1 on K).
@@ -323,7 +348,8 @@ static int decode_impl(const void* Q, const void* K, const void* V, int dtype,
   uint32_t* bits = reinterpret_cast<uint32_t*>(ws + w.bits);
   int bits_written = 0;
   if ((st = launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx, counters, s,
-                          use_union ? bits : nullptr, w.bits_stride, &bits_written)))
+                          use_union ? bits : nullptr, w.bits_stride, &bits_written,
+                          w.sel_bytes ? ws + w.sel : nullptr)))
     return st;
   if ((st = mark(2))) return st;
   if (passes < 3) return DCR_OK;
@@ -434,12 +460,14 @@ int dcr_select_indices_projected(const void* Q, const void* KP, int dtype, int64
   const WorkspaceLayout w = workspace_layout(rows, N, k_eff);
   if (workspace == nullptr || workspace_bytes < w.total) return DCR_ERR_WORKSPACE;
   if (!aligned16(workspace)) return DCR_ERR_ALIGN;
-  uint16_t* scores = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(workspace) + w.scores);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint16_t* scores = reinterpret_cast<uint16_t*>(ws + w.scores);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((st = launch_score_projected(KP, dtype, p_stride_b, p_stride_h, Q, P, qp, eps, B, H,
                                    H_kv, N, scores, w.n_pad, 1, s)))
     return st;
-  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s);
+  return launch_select(scores, w.n_pad, rows, N, k_eff, 1, idx_out, nullptr, s, nullptr, 0,
+                       nullptr, w.sel_bytes ? ws + w.sel : nullptr);
 }
 
 int dcr_decode_projected(const void* Q, const void* K, const void* V, const void* KP, int dtype,

@@ -75,6 +75,8 @@ struct WorkspaceLayout {
   size_t idx;       // int32 [rows * k_eff]
   size_t bits;      // uint32 [rows * bits_stride] selection bitmaps (union Pass 3 only)
   int64_t bits_stride;
+  size_t sel;       // the chunked Pass 2's scratch (select_stream_bytes; 0 bytes if unused)
+  size_t sel_bytes;
   size_t total;
   int splits;
   int part_splits;  // splits the partials hold (>= splits; the union Pass 3 may use more)
@@ -93,9 +95,18 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
 // bits (optional): when every thread's positions are whole 32-bit words of the row, the
 // selection is written as a bitmap [rows][bits_stride] words (bit n of word n / 32) instead
 // of the index lists, and *bits_written is set to 1; otherwise idx is written and it is 0.
+// scratch (optional, select_stream_bytes(rows, N) bytes): where select_stream_path(rows, N)
+// holds, the selection runs as the chunked kernels of dcr_select_stream.cu (bit-identical
+// output, always as bitmaps when bits is given); without it, the one-CTA-per-row kernel.
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
                   int keys_in, int32_t* idx, int* row_counters, cudaStream_t st,
-                  uint32_t* bits = nullptr, int64_t bits_stride = 0, int* bits_written = nullptr);
+                  uint32_t* bits = nullptr, int64_t bits_stride = 0, int* bits_written = nullptr,
+                  uint8_t* scratch = nullptr);
+bool select_stream_path(int rows, int N);
+size_t select_stream_bytes(int rows, int N);
+int launch_select_stream(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+                         int keys_in, int32_t* idx, int* row_counters, uint8_t* scratch,
+                         uint32_t* bits, int64_t bits_stride, cudaStream_t st);
 
 // counts (optional): row r attends to the first counts[r] of its k_eff index slots.
 // state (optional): write the unnormalised (m, l, o[D]) per row (m in base-2 units of

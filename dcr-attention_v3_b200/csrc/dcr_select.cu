@@ -359,8 +359,14 @@ static int launch_select_t(const P2Params& p, int rows, int C, cudaStream_t st) 
 
 int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
                   int keys_in, int32_t* idx, int* row_counters, cudaStream_t st, uint32_t* bits,
-                  int64_t bits_stride, int* bits_written) {
+                  int64_t bits_stride, int* bits_written, uint8_t* scratch) {
   if (bits_written != nullptr) *bits_written = 0;
+  if (scratch != nullptr && select_stream_path(rows, N)) {
+    const int e = launch_select_stream(scores, s_stride_row, rows, N, k_eff, keys_in, idx,
+                                       row_counters, scratch, bits, bits_stride, st);
+    if (e == DCR_OK && bits != nullptr && bits_written != nullptr) *bits_written = 1;
+    return e;
+  }
   // the bitmap goes out only where every thread's keys are whole aligned words
   auto with_bits = [&](P2Params& q, int vpt, int C) {
     if (bits != nullptr && vpt % 4 == 0 && (C == 1 || q.seg_vec % 4 == 0)) {

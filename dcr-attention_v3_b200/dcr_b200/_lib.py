@@ -44,6 +44,8 @@ SIGNATURES = {
     "dcr_score": (_i32, [_vp, _i32, _i64, _i64, _vp, _vp, _f32, _i32, _i32, _i32, _i32, _i32,
                          _vp, _i64, _vp]),
     "dcr_select": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "dcr_select_workspace_bytes": (_sz, [_i32, _i32]),
+    "dcr_select_ws": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _sz, _vp]),
     "dcr_attend": (_i32, [_vp, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _i32, _i32, _i32,
                           _i32, _i32, _i32, _vp, _vp, _sz, _vp]),
     "dcr_select_indices": (_i32, [_vp, _vp, _i32, _i64, _i64, _i32, _i32, _i32, _i32, _i32,

@@ -5,6 +5,8 @@ Drop-in for ``topk_pass2_select``
 positions a stable descending argsort of ``f32(scores)`` puts first (ties -> lower
 index), returned in ascending order as int32. The kernel (csrc/dcr_select.cu) finds the
 k-th largest 16-bit key by radix select and emits the set in index order, with no sort.
+Past one wave of rows (B x H x N above 148 x 32768) the same selection runs as chunked
+grid-wide kernels (csrc/dcr_select_stream.cu) over a workspace allocated here.
 """
 from __future__ import annotations
 
@@ -28,8 +30,15 @@ def topk_pass2_select(
         else scores.contiguous()
     stride = s.stride(1)
     idx = torch.empty(B, H, k_eff, dtype=torch.int32, device=scores.device)
+    lib = _lib.load()
+    ws_bytes = int(lib.dcr_select_workspace_bytes(B * H, N))
     with torch.cuda.device(scores.device):
-        st = _lib.load().dcr_select(s.data_ptr(), stride, B * H, N, int(k_eff), idx.data_ptr(),
-                                    _lib.stream_ptr(scores.device))
-    _lib.check(st, "dcr_select")
+        if ws_bytes == 0:
+            st = lib.dcr_select(s.data_ptr(), stride, B * H, N, int(k_eff), idx.data_ptr(),
+                                _lib.stream_ptr(scores.device))
+        else:
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=scores.device)
+            st = lib.dcr_select_ws(s.data_ptr(), stride, B * H, N, int(k_eff), idx.data_ptr(),
+                                   ws.data_ptr(), ws_bytes, _lib.stream_ptr(scores.device))
+    _lib.check(st, "dcr_select_ws" if ws_bytes else "dcr_select")
     return idx

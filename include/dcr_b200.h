@@ -109,6 +109,18 @@ int dcr_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_h,
 int dcr_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
                int32_t* idx_out, void* stream);
 
+/* Bytes of device workspace dcr_select_ws needs for rows x N: 0 where the one-CTA-per-row
+ * selection of dcr_select runs anyway (rows x N up to 148 x 32768), else the scratch of
+ * the chunked selection (row histograms and per-chunk counts). */
+size_t dcr_select_workspace_bytes(int rows, int N);
+
+/* dcr_select with a workspace (16-byte aligned, dcr_select_workspace_bytes bytes; it need
+ * not be zeroed): past one wave of rows the selection runs as chunked grid-wide kernels,
+ * bit-identical to dcr_select. The same replacement of topk_pass2_select
+ * (topk_axis_pass2.py:16) for large B x H x N. */
+int dcr_select_ws(const uint16_t* scores, int64_t s_stride_row, int rows, int N, int k_eff,
+                  int32_t* idx_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Pass 3: O[b, h] = softmax((K[b, h/G, idx] . f32(Q[b, h])) / sqrt(D)) @ V[b, h/G, idx],
  * fp32 online softmax, one rounding to the output dtype. idx is [B*H, k_eff] int32.
  * Replaces fused_topk_attention, dcr_attention/kernel/triton/fused_attn.py:158

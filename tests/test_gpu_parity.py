@@ -141,6 +141,9 @@ SWEEP = [
     (4, 32, 8, 40960, 6144, "f16"),      # the longest row that shape covers
     (4, 32, 8, 40961, 6144, "bf16"),     # two-CTA clusters
     (1, 4, 1, 262209, 13112, "bf16"),    # past 262144: 8-CTA clusters of 1024 threads
+    (8, 32, 8, 20000, 3000, "bf16"),     # past one wave of rows: the chunked Pass 2, bitmaps
+    (8, 32, 8, 20000, 3000, "f32"),      # the chunked Pass 2 writing index lists
+    (4, 64, 8, 20001, 3001, "f16"),      # G = 8 over the chunked selection
 ]
 
 
@@ -327,11 +330,16 @@ def _adversarial_rows(kind: str, R: int, N: int, g: torch.Generator) -> torch.Te
     ("raw_bits", 8, 5000, 2500), ("specials", 4, 3001, 1500), ("decode", 128, 32768, 4916),
     ("decode", 4, 32768, 1), ("decode", 4, 32768, 32767), ("three_values", 2, 70000, 30001),
     ("decode", 1, 300000, 45000), ("narrow", 2, 262209, 39331), ("raw_bits", 3, 65536, 9830),
+    # more keys than 148 rows of 32768: the chunked selection of dcr_select_ws
+    ("all_equal", 160, 32768, 4916), ("three_values", 64, 100000, 40000),
+    ("narrow", 32, 262209, 39331), ("specials", 160, 33001, 16500), ("decode", 256, 32768, 1),
+    ("decode", 160, 32768, 32767), ("raw_bits", 160, 32768, 9830), ("decode", 512, 32768, 4916),
 ])
 def test_pass2_adversarial_distributions(kind, R, N, k):
     """Pass 2 on score rows built to stress the radix select (ties across and inside the
-    threshold bin, every bf16 pattern, k = 1 and k = N, one- and multi-CTA rows) against
-    a stable torch sort of the same order keys: bit-exact."""
+    threshold bin, every bf16 pattern, k = 1 and k = N, one- and multi-CTA rows, and the
+    chunked grid-wide selection past one wave of rows, with ragged last chunks) against a
+    stable torch sort of the same order keys: bit-exact."""
     g = torch.Generator().manual_seed(sum(map(ord, kind)) * 7919 + R * 131 + N + k)
     scores = _adversarial_rows(kind, R, N, g).reshape(1, R, N).to(DEV)
     idx = _api().topk_pass2_select(scores, k)
