@@ -625,15 +625,8 @@ int dcr_shard_selection(const void* workspace, size_t workspace_bytes, int B, in
   if ((st = shard_ws(B, H, N_local, k_eff, const_cast<void*>(workspace), workspace_bytes, w)))
     return st;
   const uint8_t* ws = static_cast<const uint8_t*>(workspace);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const size_t rows = static_cast<size_t>(B) * H;
-  if (cudaMemcpyAsync(idx_out, ws + w.idx, sizeof(int32_t) * rows * w.cap,
-                      cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-    return DCR_ERR_CUDA;
-  if (cudaMemcpyAsync(count_out, ws + w.count, sizeof(int32_t) * rows, cudaMemcpyDeviceToDevice,
-                      s) != cudaSuccess)
-    return DCR_ERR_CUDA;
-  return DCR_OK;
+  return launch_shard_selection_out(w, ws, B * H, N_local, k_eff, idx_out, count_out,
+                                    static_cast<cudaStream_t>(stream));
 }
 
 int dcr_binary_version(int* version_out) {

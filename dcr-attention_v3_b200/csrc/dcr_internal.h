@@ -129,6 +129,7 @@ struct ShardLayout {
   size_t chunk_cnt;  // uint32 [rows * chunks]
   size_t bits;       // uint32 [rows * bits_stride] selection bitmaps (fused selection)
   int64_t bits_stride;
+  size_t mode;       // int32: 1 if the last selection wrote bitmaps only, else 0
   size_t total;
   int splits, cap, chunks;
   int part_splits;   // splits the partials hold (the union Pass 3 may use more)
@@ -155,9 +156,15 @@ int launch_shard_combine(const float* states, int world, int rows, int dtype, vo
 // resident (every rank, same GPUs, fails alike).
 // *bits_written: the selection was also written as bitmaps (w.bits; every thread's
 // positions are whole 32-bit words), which the union Pass 3 reads.
+// bits_only: where the bitmaps are written, skip the index lists (the caller's union
+// Pass 3 reads the bitmaps only; launch_shard_selection_out rebuilds the lists on request).
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
                               int n_local_max, int k_eff, const struct PeerView* pv,
-                              cudaStream_t st, bool* launched, bool* bits_written = nullptr);
+                              cudaStream_t st, bool* launched, bool* bits_written = nullptr,
+                              bool bits_only = false);
+// The last step's selection as index lists [rows][cap] and counts [rows].
+int launch_shard_selection_out(const ShardLayout& w, const uint8_t* ws, int rows, int N_local,
+                               int k_eff, int32_t* idx_out, int32_t* count_out, cudaStream_t st);
 
 // Projected-score mode (dcr_project.cu). Append: copies n_new rows of K and V into the
 // caches at position pos (k_cache may be null: no copy) and writes their projection

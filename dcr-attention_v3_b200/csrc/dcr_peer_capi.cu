@@ -127,8 +127,9 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
     return st;
   if ((st = mark(1))) return st;
   bool fused = false, bits = false;
+  const bool use_union = union_enabled() && union_supported(dtype, H, H_kv);
   if ((st = launch_shard_select_fused(w, ws, rows, N_local, n_local_max, k_eff, &v, s, &fused,
-                                      &bits)))
+                                      &bits, use_union)))
     return st;
   if (fused) {
     if ((st = mark(2)) || (st = mark(3))) return st;
@@ -146,7 +147,7 @@ static int shard_decode_peer_impl(const void* Q, const void* K, const void* V, i
   // Pass 3 publishes its states into the exchange buffers; the pointer only selects the
   // state output
   float* own_state = reinterpret_cast<float*>(v.base[rank] + v.lay.st);
-  if (fused && bits && union_enabled() && union_supported(dtype, H, H_kv)) {
+  if (fused && bits && use_union) {
     // the union Pass 3 over the fused selection's bitmaps
     if ((st = launch_attend_union(Q, K, V, dtype, k_stride_b, k_stride_h, v_stride_b, v_stride_h,
                                   reinterpret_cast<const int32_t*>(ws + w.idx),

@@ -78,6 +78,39 @@ __device__ __forceinline__ void ss_load(const SsParams& p, const uint16_t* src, 
   }
 }
 
+// A and C need no position order: thread t of the chunk's CTA takes vectors t, t + 256,
+// t + 512 and t + 768 (8 keys each), so every load instruction of a warp reads 512
+// contiguous bytes. Key 8 i + e sits at position chunk0 + 8 (256 i + t) + e.
+__device__ __forceinline__ int ss_pos(int chunk0, int i, int e) {
+  return chunk0 + 8 * (kSsThreads * i + static_cast<int>(threadIdx.x)) + e;
+}
+
+__device__ __forceinline__ void ss_load_spread(const SsParams& p, const uint16_t* src,
+                                               int chunk0, uint32_t (&key)[kSsKeys]) {
+#pragma unroll
+  for (int i = 0; i < kSsKeys / 8; ++i) {
+    const int pos0 = ss_pos(chunk0, i, 0);
+    if (p.vec && pos0 + 8 <= p.N) {
+      const uint4 w = *reinterpret_cast<const uint4*>(src + pos0);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        key[8 * i + 2 * q] = ww[q] & 0xffffu;
+        key[8 * i + 2 * q + 1] = ww[q] >> 16;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        key[8 * i + e] = pos0 + e < p.N ? static_cast<uint32_t>(src[pos0 + e]) : 0u;
+    }
+    if (!p.keys_in) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (pos0 + e < p.N) key[8 * i + e] = order_key_fast(key[8 * i + e]);
+    }
+  }
+}
+
 // A: the chunk's first-level histogram, added into the row's.
 __global__ void __launch_bounds__(kSsThreads) ss_hist_kernel(const SsParams p) {
   __shared__ uint32_t h[kSsBins1];
@@ -168,25 +201,34 @@ __global__ void __launch_bounds__(kSsThreads) ss_refine_kernel(const SsParams p)
   const int warp = tid >> 5;
   const int row = blockIdx.x / p.nchunks;
   const int c = blockIdx.x - row * p.nchunks;
+  const int chunk0 = c * kSsChunk;
   const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
   uint32_t key[kSsKeys];
-  ss_load(p, src, c * kSsChunk + tid * kSsKeys, key);
+  ss_load_spread(p, src, chunk0, key);
   if (tid < kSsBins2) h[tid] = 0u;
-  const int bh_i = p.rowinfo[row].x;
-  const uint32_t bh = static_cast<uint32_t>(bh_i);  // -1 (no bin): nothing is in or above it
+  // BH's keys are [lo16, lo16 + 15]; with no bin (-1) lo16 = 0xfffffff0 and no key is in
+  // or above it. Padding (key 0) is never in BH: a real BH is at least 0x007f >> 4.
+  const uint32_t lo16 = static_cast<uint32_t>(p.rowinfo[row].x) << 4;
+  const uint32_t hi16 = lo16 | 15u;
   __syncthreads();
-  uint32_t above = 0;
+  uint32_t above = 0, cand = 0;
 #pragma unroll
   for (int e = 0; e < kSsKeys; ++e) {
-    const uint32_t hi = key[e] >> 4;
-    above += (bh_i >= 0 && hi > bh) ? 1u : 0u;
-    const bool in_bh = bh_i >= 0 && hi == bh && key[e] != 0u;
-    if (__any_sync(0xffffffffu, in_bh)) {
-      if (in_bh) atomicAdd(&h[key[e] & 15u], 1u);
-    }
+    if (key[e] > hi16) ++above;
+    if (key[e] - lo16 < 16u) cand |= 1u << e;
   }
-  const uint32_t incl = warp_incl_scan(above);
-  if (lane == 31) wsum[warp] = incl;
+  // BH holds a few percent of the keys: each is added from its stored key, read again
+  while (cand) {
+    const int e = __ffs(cand) - 1;
+    cand &= cand - 1;
+    const int pos = ss_pos(chunk0, e >> 3, e & 7);
+    uint32_t x = src[pos];
+    if (!p.keys_in) x = order_key_fast(x);
+    atomicAdd(&h[x & 15u], 1u);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) above += __shfl_xor_sync(0xffffffffu, above, o);
+  if (lane == 0) wsum[warp] = above;
   __syncthreads();
   uint32_t* out = p.chunk + (static_cast<int64_t>(row) * p.nchunks + c) * kSsChunkWords;
   if (tid == 0) {
@@ -287,8 +329,8 @@ __global__ void __launch_bounds__(kSsThreads) ss_emit_kernel(const SsParams p) {
   uint32_t gtm = 0u, eqm = 0u;
 #pragma unroll
   for (int e = 0; e < kSsKeys; ++e) {
-    gtm |= (key[e] > T ? 1u : 0u) << e;
-    eqm |= (key[e] == T ? 1u : 0u) << e;
+    if (key[e] > T) gtm |= 1u << e;
+    if (key[e] == T) eqm |= 1u << e;
   }
   // block exclusive scan of (#gt | #eq << 16): at most 8192 of each per chunk
   const uint32_t packed = static_cast<uint32_t>(__popc(gtm)) | (static_cast<uint32_t>(__popc(eqm)) << 16);
@@ -370,11 +412,12 @@ int launch_select_stream(const uint16_t* scores, int64_t s_stride_row, int rows,
       cudaSuccess)
     return DCR_ERR_CUDA;
   const unsigned g = static_cast<unsigned>(grid);
+  const unsigned rows_grid = static_cast<unsigned>(rows);
+  const unsigned thr_grid = static_cast<unsigned>((rows + kSsThreads / 32 - 1) / (kSsThreads / 32));
   ss_hist_kernel<<<g, kSsThreads, 0, st>>>(p);
-  ss_bin_kernel<<<static_cast<unsigned>(rows), kSsThreads, 0, st>>>(p);
+  ss_bin_kernel<<<rows_grid, kSsThreads, 0, st>>>(p);
   ss_refine_kernel<<<g, kSsThreads, 0, st>>>(p);
-  ss_thresh_kernel<<<static_cast<unsigned>((rows + kSsThreads / 32 - 1) / (kSsThreads / 32)),
-                     kSsThreads, 0, st>>>(p, rows);
+  ss_thresh_kernel<<<thr_grid, kSsThreads, 0, st>>>(p, rows);
   ss_emit_kernel<<<g, kSsThreads, 0, st>>>(p);
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }

@@ -60,6 +60,8 @@ struct ShardParams {
                               // hist_hi / hist_out / hist_lo_all
   uint32_t* bits;             // optional (fused selection): [rows][bits_stride] bitmaps of the
   int64_t bits_stride;        // selected local positions, written besides idx
+  int emit_idx;               // 0: bitmaps only (the union Pass 3 reads nothing else)
+  int32_t* mode;              // [1]: 1 if the last selection wrote bitmaps only, else 0
 };
 
 // The 32 keys of this thread in chunk `chunk` of row `row`; 0 past the end of the row
@@ -257,6 +259,7 @@ __global__ void __launch_bounds__(kShThreads) shard_emit_kernel(const ShardParam
   const int chunk = blockIdx.x % p.chunks;
   const uint32_t T = static_cast<uint32_t>(p.row_state[row * 4 + 2]);
   const uint32_t quota = static_cast<uint32_t>(p.row_state[row * 4 + 3]);
+  if (blockIdx.x == 0 && tid == 0) *p.mode = 0;  // index lists
   if (warp == 0) {
     uint32_t gb = 0, eb = 0, ga = 0;
     for (int c = lane; c < p.chunks; c += 32) {
@@ -563,6 +566,7 @@ __global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardP
     // whole words (VPT a multiple of 4: positions base + 32 w start a word)
     if (p.bits != nullptr && base + 32 * w < p.N)
       p.bits[row * p.bits_stride + ((base + 32 * w) >> 5)] = sel;
+    if (!p.emit_idx) continue;
     while (sel) {
       const int bb = __ffs(sel) - 1;
       sel &= sel - 1;
@@ -574,6 +578,7 @@ __global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardP
   if (tid == 0) {
     p.count[row] = min(static_cast<int>(s_tot & 0xffffu) + quota, p.cap);
     p.counters[row] = 0;
+    if (row == 0) *p.mode = p.emit_idx ? 0 : 1;
   }
 }
 
@@ -606,6 +611,8 @@ ShardLayout shard_layout(int rows, int N_local, int k_eff) {
   w.bits = off;
   w.bits_stride = (static_cast<int64_t>(N_local) + 31) / 32;
   off = align_up_256(off + sizeof(uint32_t) * static_cast<size_t>(rows) * w.bits_stride);
+  w.mode = off;
+  off = align_up_256(off + sizeof(int32_t));
   w.total = off;
   return w;
 }
@@ -628,6 +635,8 @@ static ShardParams shard_params(const ShardLayout& w, uint8_t* ws, int rows, int
   p.counters = reinterpret_cast<int*>(ws + w.counters);
   p.bits = nullptr;
   p.bits_stride = w.bits_stride;
+  p.emit_idx = 1;
+  p.mode = reinterpret_cast<int32_t*>(ws + w.mode);
   return p;
 }
 
@@ -696,7 +705,7 @@ static int launch_fused_t(const ShardParams& p, cudaStream_t st, bool* launched)
 
 int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N_local,
                               int n_local_max, int k_eff, const PeerView* pv, cudaStream_t st,
-                              bool* launched, bool* bits_written) {
+                              bool* launched, bool* bits_written, bool bits_only) {
   *launched = false;
   if (bits_written != nullptr) *bits_written = false;
   // every rank takes the same path: decided from the longest chunk of all ranks
@@ -717,12 +726,15 @@ int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N
     return e;
   };
   if (bits_written != nullptr) p.bits = reinterpret_cast<uint32_t*>(ws + w.bits);
+  // where the bitmaps go out and the caller reads nothing else, no index lists are written
+  const int emit_idx_bits = (bits_written != nullptr && bits_only) ? 0 : 1;
   if (nvec_max > 512 * 2 && rows <= device_sm_count()) {
     const int vpt = (nvec + 1023) / 1024;
     if (vpt <= 2) {
       p.bits = nullptr;
       return launch_fused_t<2, 1024>(p, st, launched);
     }
+    p.emit_idx = emit_idx_bits;
     return with_bits(launch_fused_t<4, 1024>(p, st, launched));
   }
   const int vpt = (nvec + kFsThreads - 1) / kFsThreads;
@@ -731,8 +743,62 @@ int launch_shard_select_fused(const ShardLayout& w, uint8_t* ws, int rows, int N
     return vpt <= 1 ? launch_fused_t<1, kFsThreads>(p, st, launched)
                     : launch_fused_t<2, kFsThreads>(p, st, launched);
   }
+  p.emit_idx = emit_idx_bits;
   if (vpt <= 4) return with_bits(launch_fused_t<4, kFsThreads>(p, st, launched));
   return with_bits(launch_fused_t<8, kFsThreads>(p, st, launched));
+}
+
+// The selection of the last step as ascending index lists and counts: copied, or, where the
+// step wrote bitmaps only, rebuilt from them (one CTA per row, a block scan per 256 words).
+__global__ void __launch_bounds__(kShThreads) shard_selection_out_kernel(const ShardParams p,
+                                                                        int32_t* idx_out,
+                                                                        int32_t* count_out) {
+  __shared__ uint32_t wsum[kShWarps];
+  __shared__ uint32_t s_carry;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t row = blockIdx.x;
+  int32_t* out = idx_out + row * p.cap;
+  if (*p.mode == 0) {
+    for (int i = tid; i < p.cap; i += kShThreads) out[i] = p.idx[row * p.cap + i];
+    if (tid == 0) count_out[row] = p.count[row];
+    return;
+  }
+  if (tid == 0) s_carry = 0;
+  __syncthreads();
+  const uint32_t* brow = p.bits + row * p.bits_stride;
+  for (int64_t w0 = 0; w0 < p.bits_stride; w0 += kShThreads) {
+    const int64_t wi = w0 + tid;
+    uint32_t word = wi < p.bits_stride ? brow[wi] : 0u;
+    const uint32_t c = static_cast<uint32_t>(__popc(word));
+    const uint32_t incl = warp_incl_scan(c);
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    uint32_t pos = s_carry + incl - c;
+    for (int w = 0; w < warp; ++w) pos += wsum[w];
+    uint32_t tot = 0;
+    for (int w = 0; w < kShWarps; ++w) tot += wsum[w];
+    while (word) {
+      const int b = __ffs(word) - 1;
+      word &= word - 1;
+      if (static_cast<int>(pos) < p.cap) out[pos] = static_cast<int32_t>(wi * 32 + b);
+      ++pos;
+    }
+    __syncthreads();
+    if (tid == 0) s_carry += tot;
+    __syncthreads();
+  }
+  if (tid == 0) count_out[row] = min(static_cast<int>(s_carry), p.cap);
+}
+
+int launch_shard_selection_out(const ShardLayout& w, const uint8_t* ws, int rows, int N_local,
+                               int k_eff, int32_t* idx_out, int32_t* count_out, cudaStream_t st) {
+  ShardParams p = shard_params(w, const_cast<uint8_t*>(ws), rows, N_local, k_eff);
+  p.bits = reinterpret_cast<uint32_t*>(const_cast<uint8_t*>(ws) + w.bits);
+  shard_selection_out_kernel<<<static_cast<unsigned>(rows), kShThreads, 0, st>>>(p, idx_out,
+                                                                               count_out);
+  return check_launch();
 }
 
 int launch_shard_combine(const float* states, int world, int rows, int dtype, void* O,
