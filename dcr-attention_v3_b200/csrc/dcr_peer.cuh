@@ -184,6 +184,12 @@ __device__ __forceinline__ uint64_t ll_get_packed(const PeerView& v, const uint6
 // Reads word base[r * stride] of every rank r < world into w[r], waiting (bounded, as
 // ll_get) for each word's tag: the words are loaded together first, so a read costs one
 // round trip, not one per rank. tag_shift: 32 (full epoch) or 48 (packed 16-bit tag).
+// The polling half of ll_gather, for words already loaded once into w (full 32-bit tags):
+// re-reads only those that do not carry this step's epoch yet.
+__device__ __forceinline__ void ll_gather_late(const PeerView& v, const uint64_t* base,
+                                               int64_t stride, uint32_t epoch,
+                                               uint64_t (&w)[kMaxPeers]);
+
 __device__ __forceinline__ void ll_gather(const PeerView& v, const uint64_t* base,
                                           int64_t stride, uint32_t epoch, int tag_shift,
                                           uint64_t (&w)[kMaxPeers]) {
@@ -199,6 +205,30 @@ __device__ __forceinline__ void ll_gather(const PeerView& v, const uint64_t* bas
       __nanosleep(32);
       w[r] = ll_load(base + r * stride);
       if (static_cast<uint32_t>(w[r] >> tag_shift) == tag) break;
+      if (((++spins) & 63u) == 0u) {
+        if (ld_volatile_u32(v.abort_word()) != 0u) break;
+        if (global_timer_ns() - t0 > 2000000000ull) {
+          raise_status(DCR_ERR_DEVICE_TIMEOUT);
+          atomicExch(v.abort_word(), 1u);
+          break;
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void ll_gather_late(const PeerView& v, const uint64_t* base,
+                                               int64_t stride, uint32_t epoch,
+                                               uint64_t (&w)[kMaxPeers]) {
+#pragma unroll
+  for (int r = 0; r < kMaxPeers; ++r) {
+    if (r >= v.world || static_cast<uint32_t>(w[r] >> 32) == epoch) continue;
+    const uint64_t t0 = global_timer_ns();
+    uint32_t spins = 0;
+    while (true) {
+      __nanosleep(32);
+      w[r] = ll_load(base + r * stride);
+      if (static_cast<uint32_t>(w[r] >> 32) == epoch) break;
       if (((++spins) & 63u) == 0u) {
         if (ld_volatile_u32(v.abort_word()) != 0u) break;
         if (global_timer_ns() - t0 > 2000000000ull) {

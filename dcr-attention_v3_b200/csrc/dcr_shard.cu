@@ -334,13 +334,20 @@ __global__ void __launch_bounds__(kD) shard_combine_kernel(const float* states, 
   const uint32_t epoch = v.world > 0 ? step_epoch(v) : 0u;
   float M = -INFINITY, L = 0.0f, o = 0.0f;
   if (v.world > 0) {
-    // every rank's (m, l, o[tid]) of this row, each gathered in one round trip
+    // every rank's (m, l, o[tid]) of this row: all 3 x world words requested at once, then
+    // the late ones polled
     uint64_t wm[kMaxPeers], wl[kMaxPeers], wo[kMaxPeers];
     const int64_t stride = static_cast<int64_t>(v.rows) * kShStateFloats;
     const uint64_t* base = v.st(v.rank, 0, row);
-    ll_gather(v, base, stride, epoch, 32, wm);
-    ll_gather(v, base + 1, stride, epoch, 32, wl);
-    ll_gather(v, base + 2 + tid, stride, epoch, 32, wo);
+#pragma unroll
+    for (int r = 0; r < kMaxPeers; ++r) {
+      wm[r] = r < v.world ? ll_load(base + r * stride) : 0ull;
+      wl[r] = r < v.world ? ll_load(base + 1 + r * stride) : 0ull;
+      wo[r] = r < v.world ? ll_load(base + 2 + tid + r * stride) : 0ull;
+    }
+    ll_gather_late(v, base, stride, epoch, wm);
+    ll_gather_late(v, base + 1, stride, epoch, wl);
+    ll_gather_late(v, base + 2 + tid, stride, epoch, wo);
 #pragma unroll
     for (int r = 0; r < kMaxPeers; ++r)
       if (r < v.world) M = fmaxf(M, __uint_as_float(static_cast<uint32_t>(wm[r])));
