@@ -17,7 +17,9 @@
 //               of exact 16-bit products), scaled by 1/8 and log2(e), masked to -inf;
 //   online softmax per head in base 2 (per-warp running max and sum, merged at the end);
 //   O += P V    mma.sync m16n8k16 with P split into two 16-bit parts (hi = rn(p),
-//               lo = rn(p - hi)), so the weights keep ~16 significant bits.
+//               lo = rn(p - hi)), so the weights keep ~16 significant bits: the hi parts
+//               are A rows 0..7 and the lo parts rows 8..15 of one MMA, whose two output
+//               halves are added when the partial is written.
 // A masked row has weight exactly 0; if a V row in a warp's tile holds a non-finite value
 // (0 x inf would reach heads that did not select the row), that warp computes the tile's
 // P.V with scalar fp32 FMAs over each head's own rows instead.
@@ -140,9 +142,304 @@ __host__ __device__ constexpr int union_smem_bytes(int span, int entry_bytes) {
   return 128 + kUnStages * kUnStageBytes + span * entry_bytes;
 }
 
+// One 64-row tile of the ring for warp `warp`, which takes tile rows [16 warp, 16 warp + 16):
+// S = Q K^T on the tensor cores, the scores masked to the rows this lane's head row
+// selected (sel(r) for tile row r), online softmax in base 2, O += P V. m_run, l_part and o
+// are the warp's running state (see the kernels).
+template <typename T, typename Sel>
+__device__ __forceinline__ void union_tile(uint32_t kt, uint32_t vt, const uint32_t (&aq)[4][2],
+                                           const Sel& sel, float& m_run, float& l_part,
+                                           float (&o)[8][4]) {
+  using Mma = UnionMma<T>;
+  constexpr float kScale = 0.125f * 1.4426950408889634f;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int q4 = lane & 3;
+  const int wrow = 16 * warp;  // this warp's first row in the tile
+
+  // S = Q K^T for the warp's 16 rows (two n-tiles of 8)
+  float sacc[2][4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
+#pragma unroll
+    for (int kp = 0; kp < 2; ++kp) {
+      // matrices: rows wrow + 8j + (lane & 7), chunks 4kp + (lane >> 3)
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(kt + swz_offset(wrow + 8 * j + (lane & 7), 4 * kp + (lane >> 3), kUnTile), b0, b1,
+              b2, b3);
+      const uint32_t a0[4] = {aq[2 * kp][0], 0u, aq[2 * kp][1], 0u};
+      const uint32_t a1[4] = {aq[2 * kp + 1][0], 0u, aq[2 * kp + 1][1], 0u};
+      Mma::mma(sacc[j], a0, b0, b1);
+      Mma::mma(sacc[j], a1, b2, b3);
+    }
+  }
+
+  // mask, online softmax (per head row; the row's 16 values sit in the 4 lanes of a quad)
+  float z[2][2];
+  bool valid[2][2];
+  float tmax = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      valid[j][e] = sel(wrow + 8 * j + 2 * q4 + e);
+      z[j][e] = sacc[j][e] * kScale;
+      if (valid[j][e]) tmax = fmaxf(tmax, z[j][e]);
+    }
+  tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+  tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+  const float m_new = fmaxf(m_run, tmax);
+  float alpha = 1.0f;
+  if (m_new != -INFINITY) {
+    alpha = exp2f(m_run - m_new);  // 0 while m_run is -inf
+    m_run = m_new;
+  }
+  float pw[2][2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) pw[j][e] = valid[j][e] ? exp2f(z[j][e] - m_run) : 0.0f;
+  l_part = l_part * alpha + (pw[0][0] + pw[0][1]) + (pw[1][0] + pw[1][1]);
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    o[nt][0] *= alpha;
+    o[nt][1] *= alpha;
+    o[nt][2] *= alpha;
+    o[nt][3] *= alpha;
+  }
+
+  // V fragments of the warp's 16 rows (k) for the 8 dim tiles (n), transposed loads
+  uint32_t bv[8][2];
+#pragma unroll
+  for (int d4 = 0; d4 < 4; ++d4)
+    ldsm_x4_t(vt + swz_offset(wrow + 8 * ((lane >> 3) & 1) + (lane & 7), 2 * d4 + (lane >> 4),
+                              kUnTile),
+              bv[2 * d4][0], bv[2 * d4][1], bv[2 * d4 + 1][0], bv[2 * d4 + 1][1]);
+  uint32_t nonfin = 0u;
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    nonfin |= (bv[nt][0] & Mma::kExpMask) + Mma::kExpInc;
+    nonfin |= (bv[nt][1] & Mma::kExpMask) + Mma::kExpInc;
+  }
+  if (!__any_sync(0xffffffffu, (nonfin & 0x80008000u) != 0u)) {
+    // O += P V with P = hi + lo in one MMA: A rows 0..7 hold the heads' hi parts and rows
+    // 8..15 their lo parts, so o[.][0..1] accumulate hi . V and o[.][2..3] lo . V (summed
+    // when the partial is written)
+    uint32_t a[4];
+    Mma::split(pw[0][0], pw[0][1], a[0], a[1]);
+    Mma::split(pw[1][0], pw[1][1], a[2], a[3]);
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) Mma::mma(o[nt], a, bv[nt][0], bv[nt][1]);
+  } else {
+    // a non-finite V value in the warp's rows: each head accumulates only its own rows
+#pragma unroll 1
+    for (int kr = 0; kr < 16; ++kr) {
+      const int j = kr >> 3, c = kr & 7;
+      const int src = (lane & ~3) | (c >> 1);
+      const float w0 = __shfl_sync(0xffffffffu, j ? pw[1][0] : pw[0][0], src);
+      const float w1 = __shfl_sync(0xffffffffu, j ? pw[1][1] : pw[0][1], src);
+      const float w = (c & 1) ? w1 : w0;
+      if (!sel(wrow + kr)) continue;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const uint32_t addr = vt + swz_offset(wrow + kr, nt, kUnTile) + 4 * q4;
+        uint32_t vv;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(vv) : "r"(addr));
+        const float2 f = ElemTraits<T>::widen2(vv);
+        o[nt][0] = fmaf(w, f.x, o[nt][0]);
+        o[nt][1] = fmaf(w, f.y, o[nt][1]);
+      }
+    }
+  }
+}
+
+// Merges the 4 warps' running (m, l, o) of every head row into one partial per head,
+// [G][66] = (m, l, o[64]) at dst. Called by all threads once the ring is free (it stages the
+// warps' states there).
+__device__ __forceinline__ void union_store_partial(uint8_t* ring, int G, float m_run,
+                                                    float l_part, const float (&o)[8][4],
+                                                    float* dst) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int hr = lane >> 2;
+  const int q4 = lane & 3;
+  const bool head_ok = hr < G;
+  float* o_red = reinterpret_cast<float*>(ring);                 // [warp][G][64]
+  float* m_red = o_red + kUnWarps * kUnMaxG * kD;                // [warp][G]
+  float* l_red = m_red + kUnWarps * kUnMaxG;                     // [warp][G]
+  float lsum = l_part;
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
+  if (head_ok) {
+    float* orow = o_red + (warp * kUnMaxG + hr) * kD;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {  // the hi and lo accumulators of union_tile
+      orow[8 * nt + 2 * q4] = o[nt][0] + o[nt][2];
+      orow[8 * nt + 2 * q4 + 1] = o[nt][1] + o[nt][3];
+    }
+    if (q4 == 0) {
+      m_red[warp * kUnMaxG + hr] = m_run;
+      l_red[warp * kUnMaxG + hr] = lsum;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * (kD + 2); i += kUnThreads) {
+    const int h = i / (kD + 2), c = i - h * (kD + 2);
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kUnWarps; ++w) M = fmaxf(M, m_red[w * kUnMaxG + h]);
+    float acc = 0.0f;
+    if (c == 0) {
+      acc = M;
+    } else {
+#pragma unroll
+      for (int w = 0; w < kUnWarps; ++w) {
+        const float mw = m_red[w * kUnMaxG + h];
+        const float sc = mw == -INFINITY ? 0.0f : exp2f(mw - M);
+        acc += sc * (c == 1 ? l_red[w * kUnMaxG + h] : o_red[(w * kUnMaxG + h) * kD + c - 2]);
+      }
+    }
+    dst[h * (kD + 2) + c] = acc;
+  }
+}
+
+// The group's last CTA: folds the group's nparts partials ([nparts][G][66] floats at gpart)
+// of every head into the outputs of rows row0 .. row0 + G - 1: O (o_out), or the
+// unnormalised state (state), or, with pv.world > 0, the state published into the ranks'
+// exchange buffers. Called by all threads; the ring is free.
+template <typename T>
+__device__ __forceinline__ void union_merge(uint8_t* ring, const float* gpart, int nparts, int G,
+                                            int64_t row0, void* o_out, float* state,
+                                            const PeerView* pv) {
+  const int tid = threadIdx.x;
+  // The group's partials are one block ([nparts][G][66] floats). They are staged in the ring
+  // in chunks of up to `cap` splits (16-byte loads, up to 12 per thread in flight), and every
+  // output folds a chunk into its running (M, L, o) online: item = (head, pair of dims), `tpi`
+  // adjacent lanes per item, each taking every tpi-th split of the chunk, combined by
+  // shuffles at the end.
+  const int qs = G * (kD + 2);  // floats between consecutive splits of one head
+  const int cap = kUnStages * kUnStageBytes / 4 / qs;
+  float* sp = reinterpret_cast<float*>(ring);
+  const int items = G * (kD / 2);
+  const int tpi = items >= kUnThreads ? 1 : kUnThreads / items;  // G = 1, 2, 4, 8: 4, 2, 1, 1
+  const int rounds = (items * tpi + kUnThreads - 1) / kUnThreads;  // 2 for G = 8, else 1
+  float Mr[2] = {-INFINITY, -INFINITY}, Lr[2] = {0.0f, 0.0f};
+  float2 Ar[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+  for (int q0 = 0; q0 < nparts; q0 += cap) {
+    const int cnt = min(cap, nparts - q0);
+    const int nfl = cnt * qs;
+    const float* src = gpart + static_cast<int64_t>(q0) * qs;
+    if (q0 > 0) __syncthreads();  // the previous chunk is consumed
+    int done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {  // 264-byte splits: not always
+      const float4* src4 = reinterpret_cast<const float4*>(src);
+      float4* dst4 = reinterpret_cast<float4*>(sp);
+      const int n4 = nfl / 4;
+      for (int i0 = 0; i0 < n4; i0 += 12 * kUnThreads) {
+        float4 v[12];
+#pragma unroll
+        for (int u = 0; u < 12; ++u) {
+          const int i = i0 + u * kUnThreads + tid;
+          if (i < n4) v[u] = __ldcg(src4 + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 12; ++u) {
+          const int i = i0 + u * kUnThreads + tid;
+          if (i < n4) dst4[i] = v[u];
+        }
+      }
+      done = n4 * 4;
+    }
+    for (int i0 = done; i0 < nfl; i0 += 8 * kUnThreads) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kUnThreads + tid;
+        if (i < nfl) v[u] = __ldcg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kUnThreads + tid;
+        if (i < nfl) sp[i] = v[u];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      if (rr >= rounds) break;
+      const int item = (rr * kUnThreads + tid) / tpi;
+      if (item >= items) continue;
+      const int part = (rr * kUnThreads + tid) - item * tpi;
+      const int h = item / (kD / 2), dp = item - h * (kD / 2);
+      const float* pr = sp + h * (kD + 2);
+      // the head's maximum over the chunk (the same splits for every lane of the head)
+      float Mc = -INFINITY;
+#pragma unroll 4
+      for (int q = 0; q < cnt; ++q) Mc = fmaxf(Mc, pr[q * qs]);
+      const float Mn = fmaxf(Mr[rr], Mc);
+      if (Mn == -INFINITY) continue;  // nothing selected so far
+      const float a = Mr[rr] == -INFINITY ? 0.0f : exp2f(Mr[rr] - Mn);
+      float L = Lr[rr] * a;
+      float2 A = make_float2(Ar[rr].x * a, Ar[rr].y * a);
+#pragma unroll 4
+      for (int q = part; q < cnt; q += tpi) {
+        const float mq = pr[q * qs];
+        const float sc = mq == -INFINITY ? 0.0f : exp2f(mq - Mn);
+        const float2 ov = *reinterpret_cast<const float2*>(pr + q * qs + 2 + 2 * dp);
+        L = fmaf(sc, pr[q * qs + 1], L);
+        A.x = fmaf(sc, ov.x, A.x);
+        A.y = fmaf(sc, ov.y, A.y);
+      }
+      Mr[rr] = Mn;
+      Lr[rr] = L;
+      Ar[rr] = A;
+    }
+  }
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    if (rr >= rounds) break;
+    const int item = (rr * kUnThreads + tid) / tpi;
+    const int part = (rr * kUnThreads + tid) - item * tpi;
+    float L = Lr[rr];
+    float2 A = Ar[rr];
+    for (int o2 = 1; o2 < tpi; o2 <<= 1) {  // lanes of an item share Mr: plain sums
+      L += __shfl_xor_sync(0xffffffffu, L, o2);
+      A.x += __shfl_xor_sync(0xffffffffu, A.x, o2);
+      A.y += __shfl_xor_sync(0xffffffffu, A.y, o2);
+    }
+    if (item < items && part == 0) {
+      const int h = item / (kD / 2), dp = item - h * (kD / 2);
+      if (state == nullptr) {
+        ElemTraits<T>::store(o_out, static_cast<int>((row0 + h) * kD + 2 * dp), A.x / L);
+        ElemTraits<T>::store(o_out, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
+      } else if (pv != nullptr && pv->world > 0) {  // epoch-tagged words into slot `rank`
+        const uint32_t epoch = step_epoch(*pv);            // of every rank
+        for (int q = 0; q < pv->world; ++q) {
+          uint64_t* dst = pv->st(q, pv->rank, row0 + h);
+          ll_put(dst + 2 + 2 * dp, __float_as_uint(A.x), epoch);
+          ll_put(dst + 3 + 2 * dp, __float_as_uint(A.y), epoch);
+          if (dp == 0) {
+            ll_put(dst, __float_as_uint(Mr[rr]), epoch);
+            ll_put(dst + 1, __float_as_uint(L), epoch);
+          }
+        }
+      } else {
+        float* st = state + (row0 + h) * (kD + 2);
+        st[2 + 2 * dp] = A.x;
+        st[3 + 2 * dp] = A.y;
+        if (dp == 0) {
+          st[0] = Mr[rr];
+          st[1] = L;
+        }
+      }
+    }
+  }
+}
+
 template <typename T, typename E>
 __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const UnionParams p) {
-  using Mma = UnionMma<T>;
   extern __shared__ uint8_t un_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(un_raw) + 127) & ~static_cast<uintptr_t>(127));
@@ -173,16 +470,14 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   const int hr = lane >> 2;  // head row of this lane's accumulators (c0, c1)
   const int q4 = lane & 3;
   const bool head_ok = hr < G;
-  uint32_t aq[4][4];
+  uint32_t aq[4][2];  // A rows 8..15 (the other two registers of a fragment) are zero
   {
     const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
         static_cast<const uint8_t*>(p.q) + (row0 + (head_ok ? hr : 0)) * 128);
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       aq[kk][0] = head_ok ? __ldg(qrow + 8 * kk + q4) : 0u;      // dims 16kk + 2q4, +1
-      aq[kk][1] = 0u;
-      aq[kk][2] = head_ok ? __ldg(qrow + 8 * kk + 4 + q4) : 0u;  // dims 16kk + 8 + 2q4, +1
-      aq[kk][3] = 0u;
+      aq[kk][1] = head_ok ? __ldg(qrow + 8 * kk + 4 + q4) : 0u;  // dims 16kk + 8 + 2q4, +1
     }
   }
 
@@ -327,7 +622,6 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   float o[8][4];            // O: dim tile nt, c0/c1 = (head hr, dims 8nt + 2q4, +1)
 #pragma unroll
   for (int nt = 0; nt < 8; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.0f;
-  constexpr float kScale = 0.125f * 1.4426950408889634f;
 
   for (int tt = 0; tt < ntiles; ++tt) {
     cp_async_wait<kUnStages - 2>();
@@ -335,146 +629,19 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
     issue(tt + kUnStages - 1);
     const uint32_t kt = smem_u32(ring + (tt % kUnStages) * kUnStageBytes);
     const uint32_t vt = kt + kUnTileBytes;
-    const int wrow = 16 * warp;  // this warp's first row in the tile
+    auto sel = [&](int r) {
+      const int t = tt * kUnTile + r;
+      return head_ok && t < n_union && ((static_cast<uint32_t>(list[t]) >> (12 + hr)) & 1u);
+    };
 
-    // S = Q K^T for the warp's 16 rows (two n-tiles of 8)
-    float sacc[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.0f;
-#pragma unroll
-      for (int kp = 0; kp < 2; ++kp) {
-        // matrices: rows wrow + 8j + (lane & 7), chunks 4kp + (lane >> 3)
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kt + swz_offset(wrow + 8 * j + (lane & 7), 4 * kp + (lane >> 3), kUnTile), b0, b1,
-                b2, b3);
-        Mma::mma(sacc[j], aq[2 * kp], b0, b1);
-        Mma::mma(sacc[j], aq[2 * kp + 1], b2, b3);
-      }
-    }
-
-    // mask, online softmax (per head row; the row's 16 values sit in the 4 lanes of a quad)
-    float z[2][2];
-    bool valid[2][2];
-    float tmax = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int t = tt * kUnTile + wrow + 8 * j + 2 * q4 + e;
-        valid[j][e] = head_ok && t < n_union && ((static_cast<uint32_t>(list[t]) >> (12 + hr)) & 1u);
-        z[j][e] = sacc[j][e] * kScale;
-        if (valid[j][e]) tmax = fmaxf(tmax, z[j][e]);
-      }
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
-    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    const float m_new = fmaxf(m_run, tmax);
-    float alpha = 1.0f;
-    if (m_new != -INFINITY) {
-      alpha = exp2f(m_run - m_new);  // 0 while m_run is -inf
-      m_run = m_new;
-    }
-    float pw[2][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) pw[j][e] = valid[j][e] ? exp2f(z[j][e] - m_run) : 0.0f;
-    l_part = l_part * alpha + (pw[0][0] + pw[0][1]) + (pw[1][0] + pw[1][1]);
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      o[nt][0] *= alpha;
-      o[nt][1] *= alpha;
-    }
-
-    // V fragments of the warp's 16 rows (k) for the 8 dim tiles (n), transposed loads
-    uint32_t bv[8][2];
-#pragma unroll
-    for (int d4 = 0; d4 < 4; ++d4)
-      ldsm_x4_t(vt + swz_offset(wrow + 8 * ((lane >> 3) & 1) + (lane & 7), 2 * d4 + (lane >> 4),
-                                kUnTile),
-                bv[2 * d4][0], bv[2 * d4][1], bv[2 * d4 + 1][0], bv[2 * d4 + 1][1]);
-    uint32_t nonfin = 0u;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      nonfin |= (bv[nt][0] & Mma::kExpMask) + Mma::kExpInc;
-      nonfin |= (bv[nt][1] & Mma::kExpMask) + Mma::kExpInc;
-    }
-    if (!__any_sync(0xffffffffu, (nonfin & 0x80008000u) != 0u)) {
-      // O += P V with P = hi + lo
-      uint32_t ahi[4], alo[4];
-      Mma::split(pw[0][0], pw[0][1], ahi[0], alo[0]);
-      Mma::split(pw[1][0], pw[1][1], ahi[2], alo[2]);
-      ahi[1] = ahi[3] = alo[1] = alo[3] = 0u;
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        Mma::mma(o[nt], ahi, bv[nt][0], bv[nt][1]);
-        Mma::mma(o[nt], alo, bv[nt][0], bv[nt][1]);
-      }
-    } else {
-      // a non-finite V value in the warp's rows: each head accumulates only its own rows
-#pragma unroll 1
-      for (int kr = 0; kr < 16; ++kr) {
-        const int j = kr >> 3, c = kr & 7;
-        const int src = (lane & ~3) | (c >> 1);
-        const float w0 = __shfl_sync(0xffffffffu, j ? pw[1][0] : pw[0][0], src);
-        const float w1 = __shfl_sync(0xffffffffu, j ? pw[1][1] : pw[0][1], src);
-        const float w = (c & 1) ? w1 : w0;
-        const int t = tt * kUnTile + wrow + kr;
-        const bool sel = head_ok && t < n_union && ((static_cast<uint32_t>(list[t]) >> (12 + hr)) & 1u);
-        if (!sel) continue;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          const uint32_t addr = vt + swz_offset(wrow + kr, nt, kUnTile) + 4 * q4;
-          uint32_t vv;
-          asm volatile("ld.shared.u32 %0, [%1];" : "=r"(vv) : "r"(addr));
-          const float2 f = ElemTraits<T>::widen2(vv);
-          o[nt][0] = fmaf(w, f.x, o[nt][0]);
-          o[nt][1] = fmaf(w, f.y, o[nt][1]);
-        }
-      }
-    }
+    union_tile<T>(kt, vt, aq, sel, m_run, l_part, o);
   }
   cp_async_wait<0>();
   __syncthreads();  // the ring is free: reuse it for the warps' merge
 
   // ---- merge the 4 warps' (m, l, o) per head, then publish this range's partial ----------
-  float* o_red = reinterpret_cast<float*>(ring);                 // [warp][G][64]
-  float* m_red = o_red + kUnWarps * kUnMaxG * kD;                // [warp][G]
-  float* l_red = m_red + kUnWarps * kUnMaxG;                     // [warp][G]
-  float lsum = l_part;
-  lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-  lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);
-  if (head_ok) {
-    float* orow = o_red + (warp * kUnMaxG + hr) * kD;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      orow[8 * nt + 2 * q4] = o[nt][0];
-      orow[8 * nt + 2 * q4 + 1] = o[nt][1];
-    }
-    if (q4 == 0) {
-      m_red[warp * kUnMaxG + hr] = m_run;
-      l_red[warp * kUnMaxG + hr] = lsum;
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < G * (kD + 2); i += kUnThreads) {
-    const int h = i / (kD + 2), c = i - h * (kD + 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kUnWarps; ++w) M = fmaxf(M, m_red[w * kUnMaxG + h]);
-    float acc = 0.0f;
-    if (c == 0) {
-      acc = M;
-    } else {
-#pragma unroll
-      for (int w = 0; w < kUnWarps; ++w) {
-        const float mw = m_red[w * kUnMaxG + h];
-        const float sc = mw == -INFINITY ? 0.0f : exp2f(mw - M);
-        acc += sc * (c == 1 ? l_red[w * kUnMaxG + h] : o_red[(w * kUnMaxG + h) * kD + c - 2]);
-      }
-    }
-    p.part[((static_cast<int64_t>(g) * p.S_cap + s) * G + h) * (kD + 2) + c] = acc;
-  }
+  union_store_partial(ring, G, m_run, l_part, o,
+                      p.part + (static_cast<int64_t>(g) * p.S_cap + s) * G * (kD + 2));
 
   const int nparts = S_g;  // partials the group's last CTA merges
 
@@ -494,129 +661,8 @@ __global__ void __launch_bounds__(kUnThreads, 4) attend_union_kernel(const Union
   }
   __syncthreads();
   if (!is_last) return;
-  // The group's partials are one block ([nparts][G][66] floats). They are staged in the ring
-  // in chunks of up to `cap` splits (16-byte loads, up to 12 per thread in flight), and every
-  // output folds a chunk into its running (M, L, o) online: item = (head, pair of dims), `tpi`
-  // adjacent lanes per item, each taking every tpi-th split of the chunk, combined by
-  // shuffles at the end.
-  const int qs = G * (kD + 2);  // floats between consecutive splits of one head
-  const float* gpart = p.part + static_cast<int64_t>(g) * p.S_cap * qs;
-  const int cap = kUnStages * kUnStageBytes / 4 / qs;
-  float* sp = reinterpret_cast<float*>(ring);
-  const int items = G * (kD / 2);
-  const int tpi = items >= kUnThreads ? 1 : kUnThreads / items;  // G = 1, 2, 4, 8: 4, 2, 1, 1
-  const int rounds = (items * tpi + kUnThreads - 1) / kUnThreads;  // 2 for G = 8, else 1
-  float Mr[2] = {-INFINITY, -INFINITY}, Lr[2] = {0.0f, 0.0f};
-  float2 Ar[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
-  for (int q0 = 0; q0 < nparts; q0 += cap) {
-    const int cnt = min(cap, nparts - q0);
-    const int nfl = cnt * qs;
-    const float* src = gpart + static_cast<int64_t>(q0) * qs;
-    if (q0 > 0) __syncthreads();  // the previous chunk is consumed
-    int done = 0;
-    if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {  // 264-byte splits: not always
-      const float4* src4 = reinterpret_cast<const float4*>(src);
-      float4* dst4 = reinterpret_cast<float4*>(sp);
-      const int n4 = nfl / 4;
-      for (int i0 = 0; i0 < n4; i0 += 12 * kUnThreads) {
-        float4 v[12];
-#pragma unroll
-        for (int u = 0; u < 12; ++u) {
-          const int i = i0 + u * kUnThreads + tid;
-          if (i < n4) v[u] = __ldcg(src4 + i);
-        }
-#pragma unroll
-        for (int u = 0; u < 12; ++u) {
-          const int i = i0 + u * kUnThreads + tid;
-          if (i < n4) dst4[i] = v[u];
-        }
-      }
-      done = n4 * 4;
-    }
-    for (int i0 = done; i0 < nfl; i0 += 8 * kUnThreads) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kUnThreads + tid;
-        if (i < nfl) v[u] = __ldcg(src + i);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = i0 + u * kUnThreads + tid;
-        if (i < nfl) sp[i] = v[u];
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      if (rr >= rounds) break;
-      const int item = (rr * kUnThreads + tid) / tpi;
-      if (item >= items) continue;
-      const int part = (rr * kUnThreads + tid) - item * tpi;
-      const int h = item / (kD / 2), dp = item - h * (kD / 2);
-      const float* pr = sp + h * (kD + 2);
-      // the head's maximum over the chunk (the same splits for every lane of the head)
-      float Mc = -INFINITY;
-#pragma unroll 4
-      for (int q = 0; q < cnt; ++q) Mc = fmaxf(Mc, pr[q * qs]);
-      const float Mn = fmaxf(Mr[rr], Mc);
-      if (Mn == -INFINITY) continue;  // nothing selected so far
-      const float a = Mr[rr] == -INFINITY ? 0.0f : exp2f(Mr[rr] - Mn);
-      float L = Lr[rr] * a;
-      float2 A = make_float2(Ar[rr].x * a, Ar[rr].y * a);
-#pragma unroll 4
-      for (int q = part; q < cnt; q += tpi) {
-        const float mq = pr[q * qs];
-        const float sc = mq == -INFINITY ? 0.0f : exp2f(mq - Mn);
-        const float2 ov = *reinterpret_cast<const float2*>(pr + q * qs + 2 + 2 * dp);
-        L = fmaf(sc, pr[q * qs + 1], L);
-        A.x = fmaf(sc, ov.x, A.x);
-        A.y = fmaf(sc, ov.y, A.y);
-      }
-      Mr[rr] = Mn;
-      Lr[rr] = L;
-      Ar[rr] = A;
-    }
-  }
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    if (rr >= rounds) break;
-    const int item = (rr * kUnThreads + tid) / tpi;
-    const int part = (rr * kUnThreads + tid) - item * tpi;
-    float L = Lr[rr];
-    float2 A = Ar[rr];
-    for (int o2 = 1; o2 < tpi; o2 <<= 1) {  // lanes of an item share Mr: plain sums
-      L += __shfl_xor_sync(0xffffffffu, L, o2);
-      A.x += __shfl_xor_sync(0xffffffffu, A.x, o2);
-      A.y += __shfl_xor_sync(0xffffffffu, A.y, o2);
-    }
-    if (item < items && part == 0) {
-      const int h = item / (kD / 2), dp = item - h * (kD / 2);
-      if (p.state == nullptr) {
-        ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp), A.x / L);
-        ElemTraits<T>::store(p.o, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
-      } else if (p.pv.world > 0) {  // epoch-tagged words into slot `rank` of every rank
-        const uint32_t epoch = step_epoch(p.pv);
-        for (int q = 0; q < p.pv.world; ++q) {
-          uint64_t* dst = p.pv.st(q, p.pv.rank, row0 + h);
-          ll_put(dst + 2 + 2 * dp, __float_as_uint(A.x), epoch);
-          ll_put(dst + 3 + 2 * dp, __float_as_uint(A.y), epoch);
-          if (dp == 0) {
-            ll_put(dst, __float_as_uint(Mr[rr]), epoch);
-            ll_put(dst + 1, __float_as_uint(L), epoch);
-          }
-        }
-      } else {
-        float* st = p.state + (row0 + h) * (kD + 2);
-        st[2 + 2 * dp] = A.x;
-        st[3 + 2 * dp] = A.y;
-        if (dp == 0) {
-          st[0] = Mr[rr];
-          st[1] = L;
-        }
-      }
-    }
-  }
+  union_merge<T>(ring, p.part + static_cast<int64_t>(g) * p.S_cap * G * (kD + 2), nparts, G,
+                 row0, p.o, p.state, &p.pv);
   if (tid == 0) p.counters[g] = 0;
 }
 

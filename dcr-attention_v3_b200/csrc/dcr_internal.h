@@ -92,9 +92,10 @@ int launch_score(const void* K, int dtype, int64_t k_stride_b, int64_t k_stride_
                  uint16_t* scores, int64_t s_stride_row, int keys_out, cudaStream_t st);
 
 // keys_in != 0: the rows hold order keys (from launch_score with keys_out) not bf16 bits.
-// bits (optional): when every thread's positions are whole 32-bit words of the row, the
-// selection is written as a bitmap [rows][bits_stride] words (bit n of word n / 32) instead
-// of the index lists, and *bits_written is set to 1; otherwise idx is written and it is 0.
+// bits (optional): when the threads' positions tile the row in whole 32-bit words (8, 16
+// or a multiple of 32 positions per thread, segments starting on words), the selection is
+// written as a bitmap [rows][bits_stride] words (bit n of word n / 32) instead of the index
+// lists, and *bits_written is set to 1; otherwise idx is written and it is 0.
 // scratch (optional, select_stream_bytes(rows, N) bytes): where select_stream_path(rows, N)
 // holds, the selection runs as the chunked kernels of dcr_select_stream.cu (bit-identical
 // output, always as bitmaps when bits is given); without it, the one-CTA-per-row kernel.

@@ -300,8 +300,10 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
   int take = need - eq_before;  // ties this thread may take, lowest positions first
   const int base = v0 * 8;
   if (p.bits != nullptr) {
-    // whole words: base is a multiple of 32 (VPT % 4 == 0, segments word-aligned); a word
-    // is written by the thread whose positions start it, if it starts inside the segment
+    // Segments start on whole words. With VPT % 4 == 0 a thread's positions are whole words
+    // (base a multiple of 32), and a word is written by the thread whose positions start it,
+    // if it starts inside the segment. With 8 or 16 positions per thread, the 4 or 2
+    // adjacent lanes that share a word OR their bits together and the first one writes it.
     uint32_t* brow = p.bits + static_cast<int64_t>(row) * p.bits_stride;
 #pragma unroll
     for (int w = 0; w < kWords; ++w) {
@@ -317,8 +319,15 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
         sel |= eq & ~rem;
         take = 0;
       }
-      const int start = base + 32 * w;
-      if (start < v_end * 8 && start < N) brow[start >> 5] = sel;
+      if constexpr (kKeys < 32) {
+        uint32_t word = sel << (base & 31);
+#pragma unroll
+        for (int o = 1; o < 32 / kKeys; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+        if ((base & 31) == 0 && base < v_end * 8 && base < N) brow[base >> 5] = word;
+      } else {
+        const int start = base + 32 * w;
+        if (start < v_end * 8 && start < N) brow[start >> 5] = sel;
+      }
     }
     if (C > 1) cluster.sync();
     return;
@@ -369,7 +378,8 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   }
   // the bitmap goes out only where every thread's keys are whole aligned words
   auto with_bits = [&](P2Params& q, int vpt, int C) {
-    if (bits != nullptr && vpt % 4 == 0 && (C == 1 || q.seg_vec % 4 == 0)) {
+    if (bits != nullptr && (vpt == 1 || vpt == 2 || vpt % 4 == 0) &&
+        (C == 1 || q.seg_vec % 4 == 0)) {
       q.bits = bits;
       q.bits_stride = bits_stride;
       if (bits_written != nullptr) *bits_written = 1;
@@ -417,8 +427,14 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   }
 #endif
   const int vpt = (p.seg_vec + kP2Threads - 1) / kP2Threads;
-  if (vpt <= 1) return launch_select_t<1, kP2Threads>(p, rows, C, st);
-  if (vpt <= 2) return launch_select_t<2, kP2Threads>(p, rows, C, st);
+  if (vpt <= 1) {
+    with_bits(p, 1, C);
+    return launch_select_t<1, kP2Threads>(p, rows, C, st);
+  }
+  if (vpt <= 2) {
+    with_bits(p, 2, C);
+    return launch_select_t<2, kP2Threads>(p, rows, C, st);
+  }
   if (vpt <= 4) {
     with_bits(p, 4, C);
     return launch_select_t<4, kP2Threads>(p, rows, C, st);

@@ -178,12 +178,32 @@ def test_union_pass3_shapes_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
     _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
 
 
-def test_union_pass3_keeps_nonfinite_v_rows_to_their_heads(oracle_mod):
+@pytest.mark.parametrize("B,H,H_kv,N,k,dt", [
+    (4, 32, 8, 8192, 1229, "f16"),     # 16 positions per Pass 2 thread: words from lane pairs
+    (4, 32, 8, 4000, 600, "bf16"),     # 8 positions per thread (4 lanes a word), ragged end
+    (2, 8, 4, 4096, 614, "f16"),       # G = 2, 8-CTA clusters per row, 4 groups
+    (16, 16, 8, 512, 8, "bf16"),       # 128 small groups, more rows than SMs
+    (2, 64, 8, 8192, 1229, "bf16"),    # G = 8
+    (4, 32, 8, 1024, 1023, "f16"),     # k = N - 1: nearly every position in every union
+    (4, 32, 8, 4096, 1, "f16"),        # k = 1: at most G rows per union
+])
+def test_union_pass3_from_bitmaps_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
+    """The decode step's union Pass 3 reading the selection bitmaps that Pass 2 writes when
+    its threads hold 8 or 16 positions each (lanes sharing a word OR their bits) or whole
+    words, against the oracle: small and ragged rows, clusters, G = 2 and 8, many small
+    groups, k = N - 1 and k = 1."""
+    from dcr_b200.synthetic import make_decode_inputs
+    Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=DT[dt], seed=N + k + 2)
+    _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
+
+
+@pytest.mark.parametrize("N", [5000, 4096])  # 4096: bitmaps; 5000: index lists searched
+def test_union_pass3_keeps_nonfinite_v_rows_to_their_heads(oracle_mod, N):
     """A V row holding inf or NaN that only one head of a KV group selected reaches that
     head's output and no other (the union kernel scores every union row for all heads, so
     the rows a head did not select must not be multiplied in, not even by a weight of 0)."""
     from dcr_b200.synthetic import make_decode_inputs
-    B, H, H_kv, N, k = 2, 32, 8, 5000, 750
+    B, H, H_kv, k = 2, 32, 8, 750
     G = H // H_kv
     Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=torch.float16, seed=21)
     idx = _api().topk_qaxis_select(Q.to(DEV), K.to(DEV), k).cpu()
