@@ -176,6 +176,8 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
 // counts of keys > T and == T.
 __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardParams p) {
   __shared__ uint32_t h[256];
+  __shared__ uint32_t h_below[256];
+  __shared__ uint32_t h_mine[256];
   __shared__ uint32_t s_T;
   __shared__ uint32_t red[kShWarps];
   const int tid = threadIdx.x;
@@ -193,18 +195,31 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
     return static_cast<uint32_t>(
         __ldcg(p.hist_lo_all + (static_cast<int64_t>(r) * p.rows + row) * 256 + b));
   };
-  uint32_t tot = 0;
+  // bin tid's count summed over the ranks, over the ranks below this one, and this rank's
+  uint32_t tot = 0, below = 0, mine = 0;
   if (peer) {
     uint64_t w[kMaxPeers];
     ll_gather(p.v, p.v.hl(p.v.rank, 0, row) + tid, static_cast<int64_t>(p.v.rows) * 256, epoch,
               32, w);
 #pragma unroll
-    for (int r = 0; r < kMaxPeers; ++r)
-      if (r < p.v.world) tot += static_cast<uint32_t>(w[r]);
+    for (int r = 0; r < kMaxPeers; ++r) {
+      if (r >= p.v.world) break;
+      const uint32_t c = static_cast<uint32_t>(w[r]);
+      if (r < p.rank) below += c;
+      if (r == p.rank) mine = c;
+      tot += c;
+    }
   } else {
-    for (int r = 0; r < p.world; ++r) tot += lo(r, tid);
+    for (int r = 0; r < p.world; ++r) {
+      const uint32_t c = lo(r, tid);
+      if (r < p.rank) below += c;
+      if (r == p.rank) mine = c;
+      tot += c;
+    }
   }
   h[tid] = tot;
+  h_below[tid] = below;
+  h_mine[tid] = mine;
   uint32_t key[kShKeys];
   shard_load_keys(p, row, chunk, key);
   __syncthreads();
@@ -220,9 +235,8 @@ __global__ void __launch_bounds__(kShThreads) shard_count_kernel(const ShardPara
       }
       const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
       const int need = p.k - static_cast<int>(above + above_lo);
-      int eq_lower = 0;
-      for (int r = 0; r < p.rank; ++r) eq_lower += static_cast<int>(lo(r, bl));
-      const int eq_mine = static_cast<int>(lo(p.rank, bl));
+      const int eq_lower = static_cast<int>(h_below[bl]);
+      const int eq_mine = static_cast<int>(h_mine[bl]);
       const int quota = max(0, min(need - eq_lower, eq_mine));
       s_T = T;
       if (chunk == 0) {
@@ -395,9 +409,10 @@ constexpr int kFsThreads = 512;  // CTA size for chunks up to 8192 positions (el
 
 // Publishes this row's 256-bin histogram h (exchange x, packed words) into slot `rank` of
 // every rank's buffer and sums every rank's row into out. Block-wide; ends with a barrier.
+// lower (optional): per bin, the counts of the ranks below this one (the tie quota's input).
 __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, int64_t row,
                                                     const uint32_t* h, uint32_t* out,
-                                                    uint32_t epoch) {
+                                                    uint32_t epoch, uint32_t* lower = nullptr) {
   const int tid = threadIdx.x;
   if (tid < kPackedWords) {
     const int b = 3 * tid;
@@ -407,10 +422,15 @@ __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, in
     uint64_t w[kMaxPeers];
     ll_gather(v, (x ? v.hl(v.rank, 0, row) : v.hh(v.rank, 0, row)) + tid,
               static_cast<int64_t>(v.rows) * 256, epoch, 48, w);
-    uint32_t s0 = 0, s1 = 0, s2 = 0;
+    uint32_t s0 = 0, s1 = 0, s2 = 0, l0 = 0, l1 = 0, l2 = 0;
 #pragma unroll
     for (int r = 0; r < kMaxPeers; ++r) {
       if (r >= v.world) break;
+      if (r == v.rank) {
+        l0 = s0;
+        l1 = s1;
+        l2 = s2;
+      }
       s0 += static_cast<uint32_t>(w[r] & 0xffffu);
       s1 += static_cast<uint32_t>((w[r] >> 16) & 0xffffu);
       s2 += static_cast<uint32_t>((w[r] >> 32) & 0xffffu);
@@ -418,6 +438,11 @@ __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, in
     out[b] = s0;
     if (b + 1 < 256) out[b + 1] = s1;
     if (b + 2 < 256) out[b + 2] = s2;
+    if (lower != nullptr) {
+      lower[b] = l0;
+      if (b + 1 < 256) lower[b + 1] = l1;
+      if (b + 2 < 256) lower[b + 2] = l2;
+    }
   }
   __syncthreads();
 }
@@ -429,6 +454,7 @@ __global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardP
   constexpr int kWarpsB = TPB / 32;
   __shared__ uint32_t hist[256];
   __shared__ uint32_t hsum[256];
+  __shared__ uint32_t hlow[256];  // low-byte counts of the ranks below this one
   __shared__ uint32_t wsum[kWarpsB];
   __shared__ uint32_t s_bh, s_above, s_T, s_quota, s_tot;
   const PeerView& v = p.v;
@@ -494,7 +520,7 @@ __global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardP
   for (int e = 0; e < kKeys; ++e)
     if ((key[e] >> 8) == bh && key[e] != 0u) atomicAdd(&hist[key[e] & 0xffu], 1u);
   __syncthreads();
-  exchange_row_packed(v, 1, row, hist, hsum, epoch);
+  exchange_row_packed(v, 1, row, hist, hsum, epoch, hlow);
   __syncthreads();
   if (warp == 0) {
     int bl;
@@ -508,11 +534,7 @@ __global__ void __launch_bounds__(TPB, 1) shard_select_fused_kernel(const ShardP
       }
       const uint32_t T = (bh << 8) | static_cast<uint32_t>(bl);
       const int need = p.k - static_cast<int>(s_above + above_lo);
-      int eq_lower = 0;
-      for (int r = 0; r < rank; ++r) {
-        const uint64_t w = ll_get_packed(v, v.hl(rank, r, row) + bl / 3, epoch);
-        eq_lower += static_cast<int>((w >> (16 * (bl % 3))) & 0xffffu);
-      }
+      const int eq_lower = static_cast<int>(hlow[bl]);  // ranks below this one
       const int eq_mine = static_cast<int>(hist[bl]);
       s_T = T;
       s_quota = static_cast<uint32_t>(max(0, min(need - eq_lower, eq_mine)));
