@@ -304,7 +304,11 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
     // (base a multiple of 32), and a word is written by the thread whose positions start it,
     // if it starts inside the segment. With 8 or 16 positions per thread, the 4 or 2
     // adjacent lanes that share a word OR their bits together and the first one writes it.
+    // With 40, a thread's bits start 0, 8, 16 or 24 bits into a word and reach into the
+    // next: the CTA ORs them into its words in shared memory (the first-level histogram's,
+    // free by now) and writes them out.
     uint32_t* brow = p.bits + static_cast<int64_t>(row) * p.bits_stride;
+    uint32_t selw[kWords];
 #pragma unroll
     for (int w = 0; w < kWords; ++w) {
       uint32_t sel = gtm[w];
@@ -319,14 +323,37 @@ __global__ void __launch_bounds__(TPB, 1) select_kernel(const P2Params p) {
         sel |= eq & ~rem;
         take = 0;
       }
-      if constexpr (kKeys < 32) {
-        uint32_t word = sel << (base & 31);
+      selw[w] = sel;
+    }
+    if constexpr (kKeys == 40) {
+      constexpr int kCtaWords = TPB * kKeys / 32;  // the CTA's words (its positions / 32)
+      static_assert(kCtaWords <= kP2Bins1, "staged in the first-level histogram");
+      for (int i = tid; i < kCtaWords; i += TPB) hist_hi[i] = 0u;
+      __syncthreads();
+      const int rel = base - v_begin * 8;  // 40 tid: bits 0, 8, 16 or 24 into word rel / 32
+      const uint64_t placed =
+          (static_cast<uint64_t>(selw[0]) | (static_cast<uint64_t>(selw[1] & 0xffu) << 32))
+          << (rel & 31);
+      if (static_cast<uint32_t>(placed)) atomicOr(&hist_hi[rel >> 5], static_cast<uint32_t>(placed));
+      if (static_cast<uint32_t>(placed >> 32))
+        atomicOr(&hist_hi[(rel >> 5) + 1], static_cast<uint32_t>(placed >> 32));
+      __syncthreads();
+      const int w0 = v_begin >> 2;  // the segment's first word (segments start on words)
+      const int end = min(N, v_end * 8);
+      for (int i = tid; i < kCtaWords; i += TPB)
+        if ((w0 + i) * 32 < end) brow[w0 + i] = hist_hi[i];
+    } else {
 #pragma unroll
-        for (int o = 1; o < 32 / kKeys; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
-        if ((base & 31) == 0 && base < v_end * 8 && base < N) brow[base >> 5] = word;
-      } else {
-        const int start = base + 32 * w;
-        if (start < v_end * 8 && start < N) brow[start >> 5] = sel;
+      for (int w = 0; w < kWords; ++w) {
+        if constexpr (kKeys < 32) {
+          uint32_t word = selw[w] << (base & 31);
+#pragma unroll
+          for (int o = 1; o < 32 / kKeys; o <<= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+          if ((base & 31) == 0 && base < v_end * 8 && base < N) brow[base >> 5] = word;
+        } else {
+          const int start = base + 32 * w;
+          if (start < v_end * 8 && start < N) brow[start >> 5] = selw[w];
+        }
       }
     }
     if (C > 1) cluster.sync();
@@ -378,7 +405,7 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
   }
   // the bitmap goes out only where every thread's keys are whole aligned words
   auto with_bits = [&](P2Params& q, int vpt, int C) {
-    if (bits != nullptr && (vpt == 1 || vpt == 2 || vpt % 4 == 0) &&
+    if (bits != nullptr && (vpt == 1 || vpt == 2 || vpt == 5 || vpt % 4 == 0) &&
         (C == 1 || q.seg_vec % 4 == 0)) {
       q.bits = bits;
       q.bits_stride = bits_stride;
@@ -409,20 +436,27 @@ int launch_select(const uint16_t* scores, int64_t s_stride_row, int rows, int N,
     while (C2 < kP2MaxCluster && nvec > C2 * 1024 * 5) C2 *= 2;
     if (nvec > C2 * 1024 * 5) return DCR_ERR_SHAPE;  // more than 327680 positions per row
     p.seg_vec = (nvec + C2 - 1) / C2;
-    return launch_select_t<5, 1024>(p, rows, C2, st);  // 40 keys per thread: no bitmap
+    if ((p.seg_vec + 3) / 4 * 4 <= 1024 * 5) p.seg_vec = (p.seg_vec + 3) / 4 * 4;  // on words
+    with_bits(p, 5, C2);
+    return launch_select_t<5, 1024>(p, rows, C2, st);  // 40 keys per thread
   }
   p.seg_vec = (nvec + C - 1) / C;
+  // clustered rows: segments start on whole bitmap words (4 vectors), where that still fits
+  if (C > 1 && (p.seg_vec + 3) / 4 * 4 <= kP2Threads * 8) p.seg_vec = (p.seg_vec + 3) / 4 * 4;
 #if DCR_P2_WIDE
-  // One CTA per row and every row on its own SM: 1024 threads with half the keys each
-  // (up to 32 per thread, which fit the 64 registers a 1024-thread CTA allows).
-  if (C == 1 && rows <= sms && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4) {
+  // One CTA per row: 1024 threads with half the keys each (up to 32 per thread, which fit
+  // the 64 registers a 1024-thread CTA allows), also when the rows take several waves (256
+  // rows of 32768: 23.6 against 26.8 us with 512 threads).
+  if (C == 1 && p.seg_vec > kP2Threads * 4 && p.seg_vec <= 1024 * 4) {
     with_bits(p, 4, C);
     return launch_select_t<4, 1024>(p, rows, C, st);
   }
   // Just past 32768 positions a two-CTA cluster per row would need two waves for 128
-  // rows: one 1024-thread CTA with 40 keys per thread covers up to 40960 positions.
-  if (rows <= sms && nvec > 1024 * 4 && nvec <= 1024 * 5) {
+  // rows: one 1024-thread CTA with 40 keys per thread covers up to 40960 positions (in
+  // waves when the rows are more than the SMs).
+  if (nvec > 1024 * 4 && nvec <= 1024 * 5 && C <= 2) {
     p.seg_vec = nvec;
+    with_bits(p, 5, 1);
     return launch_select_t<5, 1024>(p, rows, 1, st);
   }
 #endif

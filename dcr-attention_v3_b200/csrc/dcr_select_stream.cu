@@ -369,7 +369,10 @@ __global__ void __launch_bounds__(kSsThreads) ss_emit_kernel(const SsParams p) {
 // more keys than 148 rows of 32768. The layout reserves the scratch from the same rule, so
 // the decision needs no device.
 bool select_stream_path(int rows, int N) {
-  return static_cast<int64_t>(rows) * N > static_cast<int64_t>(148) * 32768;
+  // Rows of up to 40960 positions take one CTA each (keys in registers): in waves they still
+  // beat the chunked kernels (256 rows of 32768: 26.7 against 36.6 us). Longer rows need
+  // clusters, whose waves lose to the chunked kernels past one wave of rows.
+  return N > 40960 && static_cast<int64_t>(rows) * N > static_cast<int64_t>(148) * 32768;
 }
 
 size_t select_stream_bytes(int rows, int N) {

@@ -186,12 +186,16 @@ def test_union_pass3_shapes_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
     (2, 64, 8, 8192, 1229, "bf16"),    # G = 8
     (4, 32, 8, 1024, 1023, "f16"),     # k = N - 1: nearly every position in every union
     (4, 32, 8, 4096, 1, "f16"),        # k = 1: at most G rows per union
+    (4, 32, 8, 32800, 4920, "bf16"),   # 40 positions per thread (a model step past 32768)
+    (1, 4, 1, 262209, 13112, "f16"),   # 40 per thread in 8-CTA clusters, segments on words
+    (2, 8, 2, 64777, 9717, "bf16"),    # clustered rows, segments rounded up to whole words
+    (1, 4, 4, 100, 15, "f16"),         # G = 1, 8-CTA clusters of which the last 4 are empty
 ])
 def test_union_pass3_from_bitmaps_vs_oracle(oracle_mod, B, H, H_kv, N, k, dt):
     """The decode step's union Pass 3 reading the selection bitmaps that Pass 2 writes when
-    its threads hold 8 or 16 positions each (lanes sharing a word OR their bits) or whole
-    words, against the oracle: small and ragged rows, clusters, G = 2 and 8, many small
-    groups, k = N - 1 and k = 1."""
+    its threads hold 8 or 16 positions each (lanes sharing a word OR their bits), 40 (ORed
+    into the CTA's words in shared memory) or whole words, against the oracle: small and
+    ragged rows, clusters, G = 1, 2 and 8, many small groups, k = N - 1 and k = 1."""
     from dcr_b200.synthetic import make_decode_inputs
     Q, K, V = make_decode_inputs(B, H, H_kv, N, dtype=DT[dt], seed=N + k + 2)
     _check_vs_oracle(oracle_mod, Q, K, V, k, dt)
