@@ -1041,24 +1041,30 @@ def model_tp_bench(dev, world, rank, steps):
     c=0.05, split by KV head over the `world` ranks (one GPU each, two NCCL all-reduces per
     layer; world 1: the unsplit model). Each step is one CUDA graph per rank (H2D tokens, 16
     layers, LM head, argmax, D2H tokens) with a host sync; `steps` timed steps follow one
-    untimed pass over the same steps; ms per step, max over ranks. Sparse (exact top-K) and
-    dense SDPA in every layer, on the same caches and weights."""
+    untimed pass over the same steps; ms per step, max over ranks. Sparse (exact top-K, and
+    projected: rank-16 keys written at append) and dense SDPA in every layer, on the same
+    caches and weights; the line's value is the exact mode's."""
     import torch
     import torch.distributed as dist
 
     from dcr_b200 import _lib
     from dcr_b200.models.llama.model import (DCRLlamaDecoder, GreedyDecodeGraphs,
                                               TPDCRLlamaDecoder)
+    from dcr_b200.synthetic import projection_matrix
     B, N0, c = 8, 262144, 0.05
     kw = dict(attention="dcr", coverage_floor=c, dtype=torch.bfloat16, device=dev, seed=0)
     model = (TPDCRLlamaDecoder(world=world, rank=rank, **kw) if world > 1
              else DCRLlamaDecoder(**kw))
-    caches = model.new_caches(B, N0 + steps + 1)
+    caches = model.new_caches(B, N0 + steps + 1, P=projection_matrix(seed=0, device=dev))
     model.prefill_synthetic(caches, N0, seed=100)
     first = torch.randint(0, model.cfg.vocab, (B,), generator=torch.Generator().manual_seed(0))
     out = {}
-    for name, attention in [("dcr_exact", "dcr"), ("dense_sdpa", "dense")]:
+    for name, attention, mode in [("dcr_exact", "dcr", "exact"),
+                                  ("dcr_projected", "dcr", "projected"),
+                                  ("dense_sdpa", "dense", "exact")]:
         model.set_attention(attention)
+        for layer in model.layers:
+            layer.self_attn.mode = mode
         for cc in caches:
             cc.length = N0
         runner = GreedyDecodeGraphs(model, caches, steps)
