@@ -52,6 +52,21 @@ struct SsParams {
   int64_t bits_stride;
 };
 
+// The five kernels run as a chain of programmatic dependent launches: each lets the next
+// one launch at its start, and each waits for the previous one (griddepcontrol.wait: that
+// grid complete and its writes visible) only before it reads that grid's results, so the
+// next kernel's CTAs load Pass 1's keys while the previous one drains.
+__device__ __forceinline__ void ss_let_next_launch() {
+#if DCR_UNION_PDL
+  asm volatile("griddepcontrol.launch_dependents;");
+#endif
+}
+__device__ __forceinline__ void ss_wait_prev() {
+#if DCR_UNION_PDL
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+
 // The 32 keys of this thread, positions [base, base + 32); 0 (below every real key) past N.
 __device__ __forceinline__ void ss_load(const SsParams& p, const uint16_t* src, int base,
                                         uint32_t (&key)[kSsKeys]) {
@@ -114,6 +129,7 @@ __device__ __forceinline__ void ss_load_spread(const SsParams& p, const uint16_t
 // A: the chunk's first-level histogram, added into the row's.
 __global__ void __launch_bounds__(kSsThreads) ss_hist_kernel(const SsParams p) {
   __shared__ uint32_t h[kSsBins1];
+  ss_let_next_launch();
   const int tid = threadIdx.x;
   const int row = blockIdx.x / p.nchunks;
   const int c = blockIdx.x - row * p.nchunks;
@@ -145,6 +161,8 @@ __global__ void __launch_bounds__(kSsThreads) ss_bin_kernel(const SsParams p) {
   const int lane = tid & 31;
   const int warp = tid >> 5;
   const int row = blockIdx.x;
+  ss_let_next_launch();
+  ss_wait_prev();  // A's row histograms
   if (tid == 0) {
     s_found = 0;
     if (p.row_counters != nullptr) p.row_counters[row] = 0;
@@ -203,9 +221,11 @@ __global__ void __launch_bounds__(kSsThreads) ss_refine_kernel(const SsParams p)
   const int c = blockIdx.x - row * p.nchunks;
   const int chunk0 = c * kSsChunk;
   const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
+  ss_let_next_launch();
   uint32_t key[kSsKeys];
-  ss_load_spread(p, src, chunk0, key);
+  ss_load_spread(p, src, chunk0, key);  // Pass 1's keys: before the wait
   if (tid < kSsBins2) h[tid] = 0u;
+  ss_wait_prev();  // B's bins
   // BH's keys are [lo16, lo16 + 15]; with no bin (-1) lo16 = 0xfffffff0 and no key is in
   // or above it. Padding (key 0) is never in BH: a real BH is at least 0x007f >> 4.
   const uint32_t lo16 = static_cast<uint32_t>(p.rowinfo[row].x) << 4;
@@ -244,7 +264,9 @@ __global__ void __launch_bounds__(kSsThreads) ss_refine_kernel(const SsParams p)
 __global__ void __launch_bounds__(kSsThreads) ss_thresh_kernel(const SsParams p, int rows) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (kSsThreads / 32) + (threadIdx.x >> 5);
+  ss_let_next_launch();
   if (row >= rows) return;
+  ss_wait_prev();  // C's chunk counts
   const int4 ri = p.rowinfo[row];
   const uint32_t* crow = p.chunk + static_cast<int64_t>(row) * p.nchunks * kSsChunkWords;
   // the row's low-bin histogram: lane l sums chunks l, l + 32, ...
@@ -321,7 +343,8 @@ __global__ void __launch_bounds__(kSsThreads) ss_emit_kernel(const SsParams p) {
   const uint16_t* src = p.scores + static_cast<int64_t>(row) * p.stride;
   const int base = c * kSsChunk + tid * kSsKeys;
   uint32_t key[kSsKeys];
-  ss_load(p, src, base, key);
+  ss_load(p, src, base, key);  // Pass 1's keys: before the wait
+  ss_wait_prev();              // D's thresholds and chunk prefixes
   const int4 ri = p.rowinfo[row];
   const int2 pre = p.chunk_pre[static_cast<int64_t>(row) * p.nchunks + c];
   const uint32_t T = static_cast<uint32_t>(ri.z);
@@ -418,10 +441,25 @@ int launch_select_stream(const uint16_t* scores, int64_t s_stride_row, int rows,
   const unsigned rows_grid = static_cast<unsigned>(rows);
   const unsigned thr_grid = static_cast<unsigned>((rows + kSsThreads / 32 - 1) / (kSsThreads / 32));
   ss_hist_kernel<<<g, kSsThreads, 0, st>>>(p);
-  ss_bin_kernel<<<rows_grid, kSsThreads, 0, st>>>(p);
-  ss_refine_kernel<<<g, kSsThreads, 0, st>>>(p);
-  ss_thresh_kernel<<<thr_grid, kSsThreads, 0, st>>>(p, rows);
-  ss_emit_kernel<<<g, kSsThreads, 0, st>>>(p);
+  // B..E: programmatic dependents of the kernel before them
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = DCR_UNION_PDL ? 1 : 0;
+  auto cfg = [&](unsigned grid) {
+    cudaLaunchConfig_t c = {};
+    c.gridDim = dim3(grid);
+    c.blockDim = dim3(kSsThreads);
+    c.stream = st;
+    c.attrs = attr;
+    c.numAttrs = 1;
+    return c;
+  };
+  cudaLaunchConfig_t cb = cfg(rows_grid), cc = cfg(g), cd = cfg(thr_grid), ce = cfg(g);
+  if (cudaLaunchKernelEx(&cb, ss_bin_kernel, p) != cudaSuccess ||
+      cudaLaunchKernelEx(&cc, ss_refine_kernel, p) != cudaSuccess ||
+      cudaLaunchKernelEx(&cd, ss_thresh_kernel, p, rows) != cudaSuccess ||
+      cudaLaunchKernelEx(&ce, ss_emit_kernel, p) != cudaSuccess)
+    return DCR_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? DCR_OK : DCR_ERR_CUDA;
 }
 

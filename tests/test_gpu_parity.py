@@ -141,9 +141,12 @@ SWEEP = [
     (4, 32, 8, 40960, 6144, "f16"),      # the longest row that shape covers
     (4, 32, 8, 40961, 6144, "bf16"),     # two-CTA clusters
     (1, 4, 1, 262209, 13112, "bf16"),    # past 262144: 8-CTA clusters of 1024 threads
-    (8, 32, 8, 20000, 3000, "bf16"),     # past one wave of rows: the chunked Pass 2, bitmaps
-    (8, 32, 8, 20000, 3000, "f32"),      # the chunked Pass 2 writing index lists
-    (4, 64, 8, 20001, 3001, "f16"),      # G = 8 over the chunked selection
+    (8, 32, 8, 20000, 3000, "bf16"),     # past one wave of rows: one CTA per row, in waves
+    (8, 32, 8, 20000, 3000, "f32"),      # the same writing index lists
+    (4, 64, 8, 20001, 3001, "f16"),      # G = 8, two waves of rows
+    (4, 32, 8, 50000, 7500, "bf16"),     # long rows past one wave: the chunked Pass 2, bitmaps
+    (2, 32, 8, 81921, 12289, "f32"),     # the chunked Pass 2 writing index lists
+    (1, 64, 8, 90000, 13500, "f16"),     # G = 8 over the chunked selection
 ]
 
 
