@@ -82,7 +82,8 @@ __device__ __forceinline__ void write_state_row(const P3Params& p, int64_t row, 
   const int tid = threadIdx.x;
   if (p.pv.world > 0) {
     const uint32_t epoch = step_epoch(p.pv);
-    for (int q = 0; q < p.pv.world; ++q) {
+    for (int i = 0; i < p.pv.world; ++i) {  // own slot first, then the next ranks in turn
+      const int q = peer_order(p.pv, i);
       uint64_t* dst = p.pv.st(q, p.pv.rank, row);
       if (tid < kD) ll_put(dst + 2 + tid, __float_as_uint(o), epoch);
       if (tid == 0) {

@@ -416,7 +416,8 @@ __device__ __forceinline__ void union_merge(uint8_t* ring, const float* gpart, i
         ElemTraits<T>::store(o_out, static_cast<int>((row0 + h) * kD + 2 * dp + 1), A.y / L);
       } else if (pv != nullptr && pv->world > 0) {  // epoch-tagged words into slot `rank`
         const uint32_t epoch = step_epoch(*pv);            // of every rank
-        for (int q = 0; q < pv->world; ++q) {
+        for (int i = 0; i < pv->world; ++i) {  // own slot first, then the next ranks
+          const int q = peer_order(*pv, i);
           uint64_t* dst = pv->st(q, pv->rank, row0 + h);
           ll_put(dst + 2 + 2 * dp, __float_as_uint(A.x), epoch);
           ll_put(dst + 3 + 2 * dp, __float_as_uint(A.y), epoch);

@@ -96,6 +96,13 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
 }
 
+// The i-th destination of a push to every rank: this rank's own slot first, then the ranks
+// after it in turn, so that the ranks' pushes do not all reach the same GPU at once.
+__device__ __forceinline__ int peer_order(const PeerView& v, int i) {
+  const int q = v.rank + i;
+  return q < v.world ? q : q - v.world;
+}
+
 // This step's epoch (1 + the steps completed on this rank; every rank agrees).
 __device__ __forceinline__ uint32_t step_epoch(const PeerView& v) {
   return ld_volatile_u32(v.epoch()) + 1u;

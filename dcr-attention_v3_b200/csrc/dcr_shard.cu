@@ -167,8 +167,10 @@ __global__ void __launch_bounds__(kShThreads) shard_hist_kernel(const ShardParam
   if (!s_last) return;
   const uint32_t val = static_cast<uint32_t>(__ldcg(dst + tid));
   dst[tid] = 0;  // every chunk CTA of the row has added: clear for the next step
-  for (int q = 0; q < p.v.world; ++q)
+  for (int i = 0; i < p.v.world; ++i) {
+    const int q = peer_order(p.v, i);
     ll_put((kLevel ? p.v.hl(q, p.v.rank, row) : p.v.hh(q, p.v.rank, row)) + tid, val, epoch);
+  }
   if (tid == 0) *p.v.ticket(kLevel, row) = 0u;
 }
 
@@ -417,8 +419,10 @@ __device__ __forceinline__ void exchange_row_packed(const PeerView& v, int x, in
   if (tid < kPackedWords) {
     const int b = 3 * tid;
     const uint32_t c0 = h[b], c1 = b + 1 < 256 ? h[b + 1] : 0u, c2 = b + 2 < 256 ? h[b + 2] : 0u;
-    for (int q = 0; q < v.world; ++q)
+    for (int i = 0; i < v.world; ++i) {
+      const int q = peer_order(v, i);
       ll_put_packed((x ? v.hl(q, v.rank, row) : v.hh(q, v.rank, row)) + tid, c0, c1, c2, epoch);
+    }
     uint64_t w[kMaxPeers];
     ll_gather(v, (x ? v.hl(v.rank, 0, row) : v.hh(v.rank, 0, row)) + tid,
               static_cast<int64_t>(v.rows) * 256, epoch, 48, w);
